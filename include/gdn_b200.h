@@ -1,0 +1,189 @@
+/*
+ * gdn_b200.h — C ABI of the B200-native GatedDeltaNet (GDN) layer kernels.
+ *
+ * The library (libgdn_b200.so) replaces the GPU kernels the reference's
+ * Qwen3.5 GatedDeltaNet layer launches (sileaver/nano-vllm-extend,
+ * nanovllm/models/qwen3_5.py).  Each entry point below names the reference
+ * function it stands in for.  Conventions shared by every entry point:
+ *
+ *  - Pointers are CUDA device pointers unless stated otherwise; the caller
+ *    owns all memory.  No entry point allocates device memory, synchronises
+ *    the device or the stream, or keeps a pointer after it returns, so every
+ *    call can be captured into a CUDA graph.
+ *  - `stream` is a cudaStream_t passed as void* (NULL = legacy stream).
+ *    Work is launched on it asynchronously.
+ *  - Strides are in ELEMENTS of the pointed-to type, never bytes.
+ *  - Activations are bf16 (the reference's model dtype); recurrent states
+ *    and the log-decay g are fp32, as in the reference's state pool
+ *    (engine/model_runner.py:265-303).
+ *  - Pool arguments are the per-layer views the reference binds to each
+ *    layer (module.s_cache / module.conv_cache, model_runner.py:301-303):
+ *    the base pointer of slot 0 of that layer plus the distance between
+ *    consecutive slots (`slot_stride`).  `num_slots` counts every addressable
+ *    slot, the engine's dummy slot included.
+ *  - `ids` are int64 slot ids (context.linear_state_ids, utils/context.py:24).
+ *    A slot id outside [0, num_slots) is never dereferenced: its row is
+ *    skipped and GDN_STATUS_BAD_SLOT is OR-ed into *status (if non-NULL).
+ *    Duplicate ids in one call are undefined behaviour, as in the reference.
+ *  - Return value: GDN_OK, or an error code with a message available from
+ *    gdn_last_error() (thread-local).  Argument errors are detected on the
+ *    host before any launch, mirroring the reference's asserts.
+ */
+#ifndef GDN_B200_H_
+#define GDN_B200_H_
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define GDN_ABI_VERSION 1
+
+enum gdn_status_code {
+  GDN_OK = 0,
+  GDN_ERR_INVALID_ARGUMENT = 1, /* shape / stride / alignment contract violated */
+  GDN_ERR_UNSUPPORTED = 2,      /* valid, but not a configuration this build supports */
+  GDN_ERR_CUDA = 3              /* a CUDA runtime call or launch failed */
+};
+
+/* Bits OR-ed into the optional device status word by kernels. */
+#define GDN_STATUS_BAD_SLOT 0x1
+#define GDN_STATUS_BAD_SEQLEN 0x2
+
+enum gdn_dtype { GDN_DTYPE_F32 = 0, GDN_DTYPE_BF16 = 1 };
+
+/* Version of this ABI (GDN_ABI_VERSION of the build). */
+int gdn_abi_version(void);
+
+/* Message of the last failed call on this host thread ("" if none). */
+const char* gdn_last_error(void);
+
+/*
+ * (b) Fused gate.  Replaces fused_g_beta / _gdn_g_beta_kernel
+ * (qwen3_5.py:320-360).
+ *   g[r,h]    = -exp(a_log[h]) * softplus(a[r,h] + dt_bias[h])   (fp32;
+ *               softplus(z) = z for z > 20, else log(1 + exp(z)));
+ *               0 where row_mask[r] == 0
+ *   beta[r,h] = sigmoid(b[r,h])                                  (bf16)
+ * b, a: bf16 [n_rows, num_v_heads] with row stride ab_row_stride;
+ * a_log, dt_bias: [num_v_heads] of param_dtype (GDN_DTYPE_F32 / _BF16);
+ * row_mask: uint8 [n_rows] or NULL; g: fp32 [n_rows, num_v_heads] and
+ * beta: bf16 [n_rows, num_v_heads], both contiguous.
+ */
+int gdn_fused_g_beta(const void* b, const void* a, int64_t ab_row_stride,
+                     int64_t n_rows, int32_t num_v_heads,
+                     const void* a_log, const void* dt_bias, int32_t param_dtype,
+                     const uint8_t* row_mask, float* g, void* beta,
+                     void* stream);
+
+/*
+ * (a) Single-token causal conv + SiLU, state rolled in place by slot.
+ * Replaces conv_decode_step / _conv_decode_step_kernel (qwen3_5.py:515-558).
+ *   y[n,c] = silu(x[n,c]*w[c,K-1] + sum_{i<K-1} s[c,i]*w[c,i]),
+ *   s <- [s[1..K-2], x]     with s = conv_pool[ids[n]] ([channels, K-1]).
+ * x: bf16 [n, channels], row stride x_row_stride; conv_pool: bf16 per-layer
+ * view, taps contiguous (channel stride K-1); weight: bf16 [channels, K]
+ * contiguous (conv1d.weight); y: bf16 [n, channels], row stride y_row_stride.
+ * kernel (K) must be 2, 3 or 4.
+ */
+int gdn_conv_decode_step(const void* x, int64_t x_row_stride,
+                         void* conv_pool, int64_t slot_stride, int64_t num_slots,
+                         const int64_t* ids, int32_t n, int32_t channels,
+                         int32_t kernel, const void* weight,
+                         void* y, int64_t y_row_stride,
+                         int32_t* status, void* stream);
+
+/*
+ * (a) Varlen causal conv + SiLU with the prefix state read from, and the
+ * final state written back to, each sequence's slot.  Replaces
+ * causal_conv_silu_varlen / _causal_conv_silu_varlen_kernel
+ * (qwen3_5.py:402-473) together with the gather/scatter of the slot states
+ * around it (qwen3_5.py:941-946), and the padded variant's role
+ * (qwen3_5.py:249-317, 1048-1056).  Sequence r owns rows
+ * [cu_seqlens[r], cu_seqlens[r+1]) of x and y; cu_seqlens is int32
+ * [n_seqs + 1] on the device, non-decreasing, cu_seqlens[n_seqs] ==
+ * n_tokens.  Zero-length sequences leave their slot unchanged.  Unlike the
+ * reference kernel there is no channels % 3 restriction and y keeps the
+ * [n_tokens, channels] layout (row stride y_row_stride).
+ */
+int gdn_causal_conv_silu_varlen(const void* x, int64_t x_row_stride,
+                                void* conv_pool, int64_t slot_stride,
+                                int64_t num_slots, const int64_t* ids,
+                                const int32_t* cu_seqlens, int32_t n_seqs,
+                                int64_t n_tokens, int32_t channels,
+                                int32_t kernel, const void* weight,
+                                void* y, int64_t y_row_stride,
+                                int32_t* status, void* stream);
+
+/*
+ * (d) One decode step of the gated delta rule, state updated in place in
+ * its pool slot (no gather / scatter).  Replaces recurrent_gdn_inplace /
+ * _recurrent_inplace_kernel (qwen3_5.py:561-613) and the torch recurrence it
+ * mirrors (qwen3_5.py:616-651).  For sequence b and v-head h (k-head
+ * hk = h / (num_v_heads / num_k_heads), the reference's repeat_interleave):
+ *   q^ = l2norm(q[b,hk]) * scale,  k^ = l2norm(k[b,hk])   (eps 1e-6)
+ *   S  = s_pool[ids[b], h] * exp(g[b,h])
+ *   d  = beta[b,h] * (v[b,h] - S^T k^);  S += k^ (x) d;  out[b,h] = S^T q^
+ * q, k: bf16 rows of num_k_heads*head_k_dim; v: bf16 rows of
+ * num_v_heads*head_v_dim (each with its own row stride, heads contiguous);
+ * g: fp32 [bs, num_v_heads]; beta: bf16 [bs, num_v_heads] (both contiguous);
+ * s_pool: fp32 per-layer view [slots, num_v_heads, head_k_dim, head_v_dim]
+ * (head, row and column strides dense, as the reference asserts);
+ * out: bf16 [bs, num_v_heads, head_v_dim] contiguous.
+ * Supported head dims: (head_k_dim, head_v_dim) in {(64,64), (128,128)}.
+ */
+int gdn_recurrent_inplace(const void* q, int64_t q_row_stride,
+                          const void* k, int64_t k_row_stride,
+                          const void* v, int64_t v_row_stride,
+                          const float* g, const void* beta,
+                          float* s_pool, int64_t slot_stride, int64_t num_slots,
+                          const int64_t* ids, void* out,
+                          int32_t bs, int32_t num_k_heads, int32_t num_v_heads,
+                          int32_t head_k_dim, int32_t head_v_dim, float scale,
+                          int32_t* status, void* stream);
+
+/*
+ * (c) Varlen chunked gated-delta-rule prefill.  Replaces the chunk rule
+ * (chunk_gated_delta_rule -> fla or _torch_chunk_gated_delta_rule,
+ * qwen3_5.py:140-227) together with the slot gather/scatter around it
+ * (qwen3_5.py:956-961, 1039-1040, 1077): each sequence's initial state is
+ * read from s_pool[ids[r]] and its final state written back there.
+ * Layouts as gdn_recurrent_inplace, with q/k/v/g/beta/out holding n_tokens
+ * rows (out: bf16 [n_tokens, num_v_heads, head_v_dim] contiguous).
+ * max_seqlen bounds the longest sequence (context.max_seqlen_q); a longer
+ * sequence is truncated to max_seqlen and flagged GDN_STATUS_BAD_SEQLEN.
+ * Chunk size 64, as the reference.  Supported head dims as
+ * gdn_recurrent_inplace.
+ */
+int gdn_chunk_prefill_varlen(const void* q, int64_t q_row_stride,
+                             const void* k, int64_t k_row_stride,
+                             const void* v, int64_t v_row_stride,
+                             const float* g, const void* beta,
+                             float* s_pool, int64_t slot_stride, int64_t num_slots,
+                             const int64_t* ids, const int32_t* cu_seqlens,
+                             int32_t n_seqs, int64_t n_tokens, int32_t max_seqlen,
+                             void* out, int32_t num_k_heads, int32_t num_v_heads,
+                             int32_t head_k_dim, int32_t head_v_dim, float scale,
+                             int32_t* status, void* stream);
+
+/*
+ * Gated RMSNorm over the value head dim.  Replaces Qwen3_5RMSNormGated /
+ * _rms_gated_forward (qwen3_5.py:121-131, 697-709), with its rounding:
+ *   t = bf16(x * rsqrt(mean(x^2) + eps)); u = bf16(weight * t);
+ *   y = bf16(u * silu(gate))                      (fp32 arithmetic)
+ * x: bf16 [n_rows, dim] contiguous, n_rows = tokens * heads_per_token;
+ * gate: bf16, row r = (token t, head hh) at gate[t*gate_token_stride +
+ * hh*dim] (a [tokens, heads, dim] view whose token stride may exceed
+ * heads*dim, e.g. a column slice of a fused projection output);
+ * weight: bf16 [dim]; y: bf16 [n_rows, dim] contiguous.
+ */
+int gdn_rms_norm_gated(const void* x, const void* gate, int64_t gate_token_stride,
+                       int32_t heads_per_token, const void* weight, void* y,
+                       int64_t n_rows, int32_t dim, float eps, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* GDN_B200_H_ */

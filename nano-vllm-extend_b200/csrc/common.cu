@@ -1,0 +1,46 @@
+// Error plumbing and device queries shared by every entry point.
+#include <stdarg.h>
+#include <stdio.h>
+
+#include "common.cuh"
+
+namespace gdn {
+
+static thread_local char g_last_error[1024] = {0};
+
+void set_error(const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_last_error, sizeof(g_last_error), fmt, ap);
+  va_end(ap);
+}
+
+void clear_error() { g_last_error[0] = 0; }
+
+int check_launch(const char* what) {
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    set_error("%s: CUDA launch failed: %s", what, cudaGetErrorString(e));
+    return GDN_ERR_CUDA;
+  }
+  return GDN_OK;
+}
+
+int sm_count() {
+  static int cached[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+  if (cached[dev] == 0) {
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0)
+      n = 148;
+    cached[dev] = n;
+  }
+  return cached[dev];
+}
+
+}  // namespace gdn
+
+extern "C" int gdn_abi_version(void) { return GDN_ABI_VERSION; }
+
+extern "C" const char* gdn_last_error(void) { return gdn::g_last_error; }

@@ -1,0 +1,311 @@
+// (a) Depthwise causal conv1d + SiLU with the prefix state kept in pool slots.
+//
+// Layouts (the reference engine's, model_runner.py:265-303):
+//   x, y        bf16 [rows, C]          row strides given
+//   conv_pool   bf16 per-layer view     slot s, channel c, tap j at
+//                                       pool[s*slot_stride + c*(K-1) + j]
+//   weight      bf16 [C, K]             conv1d.weight viewed [C, K]
+//
+// Every kernel moves 8 channels per thread as one 16-byte vector (x, y, the
+// K-1 taps of 8 channels = (K-1) x 16 bytes, and the K weights of 8 channels
+// = K x 16 bytes), so a warp reads 512 contiguous bytes of a token row per
+// access.  A scalar kernel covers layouts that are not 16-byte aligned.
+//
+// The varlen prefill is split in two launches to stay race-free: the conv
+// kernel tiles the flat token axis (any number of CTAs per sequence) and only
+// READS the prefix state; a second, tiny kernel then rolls each sequence's
+// state to its last K-1 inputs.  A single launch would let the CTA holding a
+// sequence's tail overwrite the state before the CTA holding its head has
+// read it.
+#include "common.cuh"
+
+namespace gdn {
+
+constexpr int kConvThreads = 128;  // 128 threads x 8 channels = 1024 channels per CTA
+constexpr int kConvTileTokens = 32;
+
+// ---------------------------------------------------------------------------
+// single-token decode step: qwen3_5.py:515-558
+// ---------------------------------------------------------------------------
+template <int K>
+__global__ void __launch_bounds__(kConvThreads) conv_decode_vec_kernel(
+    const bf16* __restrict__ x, int64_t xs, bf16* __restrict__ pool, int64_t slot_stride,
+    int64_t num_slots, const int64_t* __restrict__ ids, int C, const bf16* __restrict__ w,
+    bf16* __restrict__ y, int64_t ys, int32_t* status) {
+  const int n = blockIdx.y;
+  const int c0 = (blockIdx.x * kConvThreads + threadIdx.x) * 8;
+  const int64_t slot = ids[n];
+  if (!slot_ok(slot, num_slots, status)) return;
+  if (c0 >= C) return;
+  constexpr int T = K - 1;
+  float xv[8], sv[8 * T], wv[8 * K], acc[8];
+  unpack8(*reinterpret_cast<const uint4*>(x + n * xs + c0), xv);
+  uint4* sp = reinterpret_cast<uint4*>(pool + slot * slot_stride + (int64_t)c0 * T);
+  uint4 sraw[T];
+#pragma unroll
+  for (int j = 0; j < T; ++j) sraw[j] = sp[j];
+#pragma unroll
+  for (int j = 0; j < T; ++j) unpack8(sraw[j], sv + 8 * j);
+  const uint4* wp = reinterpret_cast<const uint4*>(w + (int64_t)c0 * K);
+#pragma unroll
+  for (int j = 0; j < K; ++j) unpack8(wp[j], wv + 8 * j);
+#pragma unroll
+  for (int ch = 0; ch < 8; ++ch) {
+    float a = xv[ch] * wv[ch * K + (K - 1)];
+#pragma unroll
+    for (int i = 0; i < T; ++i) a += sv[ch * T + i] * wv[ch * K + i];
+    acc[ch] = siluf_(a);
+  }
+  *reinterpret_cast<uint4*>(y + n * ys + c0) = pack8(acc);
+  // roll: [s1 .. s_{T-1}, x]  (bit copies of bf16 values)
+  float ns[8 * T];
+#pragma unroll
+  for (int ch = 0; ch < 8; ++ch) {
+#pragma unroll
+    for (int i = 0; i + 1 < T; ++i) ns[ch * T + i] = sv[ch * T + i + 1];
+    ns[ch * T + T - 1] = xv[ch];
+  }
+#pragma unroll
+  for (int j = 0; j < T; ++j) sp[j] = pack8(ns + 8 * j);
+}
+
+template <int K>
+__global__ void __launch_bounds__(kConvThreads) conv_decode_scalar_kernel(
+    const bf16* __restrict__ x, int64_t xs, bf16* __restrict__ pool, int64_t slot_stride,
+    int64_t num_slots, const int64_t* __restrict__ ids, int C, const bf16* __restrict__ w,
+    bf16* __restrict__ y, int64_t ys, int32_t* status) {
+  const int n = blockIdx.y;
+  const int c = blockIdx.x * kConvThreads + threadIdx.x;
+  const int64_t slot = ids[n];
+  if (!slot_ok(slot, num_slots, status)) return;
+  if (c >= C) return;
+  constexpr int T = K - 1;
+  bf16* sp = pool + slot * slot_stride + (int64_t)c * T;
+  const bf16 xb = x[n * xs + c];
+  float s[T];
+#pragma unroll
+  for (int i = 0; i < T; ++i) s[i] = bf2f(sp[i]);
+  float a = bf2f(xb) * bf2f(w[(int64_t)c * K + K - 1]);
+#pragma unroll
+  for (int i = 0; i < T; ++i) a += s[i] * bf2f(w[(int64_t)c * K + i]);
+  y[n * ys + c] = f2bf(siluf_(a));
+#pragma unroll
+  for (int i = 0; i + 1 < T; ++i) sp[i] = sp[i + 1];
+  sp[T - 1] = xb;
+}
+
+// ---------------------------------------------------------------------------
+// varlen prefill: qwen3_5.py:402-456 (values), tiled over the flat token axis
+// ---------------------------------------------------------------------------
+
+// Sequence holding flat row t: largest r with cu[r] <= t (cu non-decreasing).
+__device__ __forceinline__ int find_seq(const int32_t* __restrict__ cu, int n_seqs, int64_t t) {
+  int lo = 0, hi = n_seqs - 1;
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if ((int64_t)cu[mid] <= t) lo = mid; else hi = mid - 1;
+  }
+  return lo;
+}
+
+template <int K, bool VEC>
+__global__ void __launch_bounds__(kConvThreads) conv_varlen_kernel(
+    const bf16* __restrict__ x, int64_t xs, const bf16* __restrict__ pool, int64_t slot_stride,
+    int64_t num_slots, const int64_t* __restrict__ ids, const int32_t* __restrict__ cu,
+    int n_seqs, int64_t n_tokens, int C, const bf16* __restrict__ w, bf16* __restrict__ y,
+    int64_t ys, int32_t* status) {
+  constexpr int T = K - 1;
+  constexpr int V = VEC ? 8 : 1;  // channels per thread
+  const int c0 = (blockIdx.y * kConvThreads + threadIdx.x) * V;
+  const int64_t t_begin = (int64_t)blockIdx.x * kConvTileTokens;
+  if (c0 >= C || t_begin >= n_tokens) return;
+  const int64_t t_end = min(t_begin + (int64_t)kConvTileTokens, n_tokens);
+
+  float wv[V * K];
+  if constexpr (VEC) {
+    const uint4* wp = reinterpret_cast<const uint4*>(w + (int64_t)c0 * K);
+#pragma unroll
+    for (int j = 0; j < K; ++j) unpack8(wp[j], wv + 8 * j);
+  } else {
+#pragma unroll
+    for (int i = 0; i < K; ++i) wv[i] = bf2f(w[(int64_t)c0 * K + i]);
+  }
+
+  int r = find_seq(cu, n_seqs, t_begin);
+  int64_t seq_start = cu[r], seq_end = cu[r + 1];
+  while (t_begin >= seq_end && r + 1 < n_seqs) {  // skip empty sequences
+    ++r; seq_start = cu[r]; seq_end = cu[r + 1];
+  }
+  float win[T][V];  // win[j] = input at position t-T+j
+  bool need_init = true;
+  for (int64_t t = t_begin; t < t_end; ++t) {
+    while (t >= seq_end && r + 1 < n_seqs) {
+      ++r; seq_start = cu[r]; seq_end = cu[r + 1]; need_init = true;
+    }
+    if (need_init) {
+      if (seq_start < 0 || seq_end > n_tokens || seq_end < seq_start) {
+        if (status) atomicOr(status, GDN_STATUS_BAD_SEQLEN);  // malformed cu_seqlens
+        return;
+      }
+      // Window for token t: positions t-T .. t-1 of sequence r; positions
+      // before the sequence start come from the slot's prefix state.
+      const int64_t slot = ids[r];
+      const bool ok = slot_ok(slot, num_slots, status);
+#pragma unroll
+      for (int j = 0; j < T; ++j) {
+        const int64_t p = t - T + j;
+        if (p >= seq_start) {
+          if constexpr (VEC) unpack8(*reinterpret_cast<const uint4*>(x + p * xs + c0), win[j]);
+          else win[j][0] = bf2f(x[p * xs + c0]);
+        } else {
+          const int tap = (int)(p - seq_start + T);  // in [0, T)
+#pragma unroll
+          for (int ch = 0; ch < V; ++ch)
+            win[j][ch] = ok ? bf2f(pool[slot * slot_stride + (int64_t)(c0 + ch) * T + tap]) : 0.f;
+        }
+      }
+      need_init = false;
+    }
+    float xv[V];
+    if constexpr (VEC) unpack8(*reinterpret_cast<const uint4*>(x + t * xs + c0), xv);
+    else xv[0] = bf2f(x[t * xs + c0]);
+    float out[V];
+#pragma unroll
+    for (int ch = 0; ch < V; ++ch) {
+      float a = 0.f;
+#pragma unroll
+      for (int i = 0; i < T; ++i) a += win[i][ch] * wv[ch * K + i];
+      a += xv[ch] * wv[ch * K + T];
+      out[ch] = siluf_(a);
+    }
+    if constexpr (VEC) *reinterpret_cast<uint4*>(y + t * ys + c0) = pack8(out);
+    else y[t * ys + c0] = f2bf(out[0]);
+#pragma unroll
+    for (int j = 0; j + 1 < T; ++j)
+#pragma unroll
+      for (int ch = 0; ch < V; ++ch) win[j][ch] = win[j + 1][ch];
+#pragma unroll
+    for (int ch = 0; ch < V; ++ch) win[T - 1][ch] = xv[ch];
+  }
+}
+
+// New state of sequence r = last K-1 entries of [old state | x rows]
+// (qwen3_5.py:450-456).  Launched after conv_varlen_kernel on the same stream.
+template <int K>
+__global__ void __launch_bounds__(kConvThreads) conv_state_writeback_kernel(
+    const bf16* __restrict__ x, int64_t xs, bf16* __restrict__ pool, int64_t slot_stride,
+    int64_t num_slots, const int64_t* __restrict__ ids, const int32_t* __restrict__ cu, int C,
+    int64_t n_tokens) {
+  constexpr int T = K - 1;
+  const int r = blockIdx.y;
+  const int c = blockIdx.x * kConvThreads + threadIdx.x;
+  if (c >= C) return;
+  const int64_t slot = ids[r];
+  if (slot < 0 || slot >= num_slots) return;  // flagged by the conv kernel
+  const int64_t start = cu[r], len = (int64_t)cu[r + 1] - start;
+  if (len <= 0 || start < 0 || start + len > n_tokens) return;  // flagged by the conv kernel
+  bf16* sp = pool + slot * slot_stride + (int64_t)c * T;
+  bf16 old[T], nw[T];
+#pragma unroll
+  for (int j = 0; j < T; ++j) old[j] = sp[j];
+#pragma unroll
+  for (int j = 0; j < T; ++j) {
+    const int64_t p = len - T + j;  // position within the sequence
+    nw[j] = p >= 0 ? x[(start + p) * xs + c] : old[p + T];
+  }
+#pragma unroll
+  for (int j = 0; j < T; ++j) sp[j] = nw[j];
+}
+
+}  // namespace gdn
+
+using namespace gdn;
+
+extern "C" int gdn_conv_decode_step(const void* x, int64_t x_row_stride, void* conv_pool,
+                                    int64_t slot_stride, int64_t num_slots, const int64_t* ids,
+                                    int32_t n, int32_t channels, int32_t kernel,
+                                    const void* weight, void* y, int64_t y_row_stride,
+                                    int32_t* status, void* stream) {
+  clear_error();
+  GDN_REQUIRE(n >= 0 && channels > 0, "gdn_conv_decode_step: bad sizes (n=%d, channels=%d)", n,
+              channels);
+  GDN_UNSUPPORTED(kernel >= 2 && kernel <= 4, "gdn_conv_decode_step: kernel %d unsupported (2..4)",
+                  kernel);
+  GDN_REQUIRE(x_row_stride >= channels && y_row_stride >= channels,
+              "gdn_conv_decode_step: row stride smaller than channels");
+  GDN_REQUIRE(num_slots > 0 && slot_stride >= (int64_t)channels * (kernel - 1),
+              "gdn_conv_decode_step: slot_stride %lld < channels*(K-1)", (long long)slot_stride);
+  if (n == 0) return GDN_OK;
+  GDN_REQUIRE(x && conv_pool && ids && weight && y, "gdn_conv_decode_step: null pointer");
+  const bool vec = channels % 8 == 0 && x_row_stride % 8 == 0 && y_row_stride % 8 == 0 &&
+                   slot_stride % 8 == 0 && aligned16(x) && aligned16(y) && aligned16(conv_pool) &&
+                   aligned16(weight);
+  cudaStream_t s = (cudaStream_t)stream;
+  const int per_cta = vec ? kConvThreads * 8 : kConvThreads;
+  dim3 grid((channels + per_cta - 1) / per_cta, n);
+#define GDN_DEC(KK)                                                                            \
+  if (kernel == KK) {                                                                          \
+    if (vec)                                                                                   \
+      conv_decode_vec_kernel<KK><<<grid, kConvThreads, 0, s>>>(                                \
+          (const bf16*)x, x_row_stride, (bf16*)conv_pool, slot_stride, num_slots, ids, channels, \
+          (const bf16*)weight, (bf16*)y, y_row_stride, status);                                \
+    else                                                                                       \
+      conv_decode_scalar_kernel<KK><<<grid, kConvThreads, 0, s>>>(                             \
+          (const bf16*)x, x_row_stride, (bf16*)conv_pool, slot_stride, num_slots, ids, channels, \
+          (const bf16*)weight, (bf16*)y, y_row_stride, status);                                \
+  }
+  GDN_DEC(2) GDN_DEC(3) GDN_DEC(4)
+#undef GDN_DEC
+  return check_launch("gdn_conv_decode_step");
+}
+
+extern "C" int gdn_causal_conv_silu_varlen(const void* x, int64_t x_row_stride, void* conv_pool,
+                                           int64_t slot_stride, int64_t num_slots,
+                                           const int64_t* ids, const int32_t* cu_seqlens,
+                                           int32_t n_seqs, int64_t n_tokens, int32_t channels,
+                                           int32_t kernel, const void* weight, void* y,
+                                           int64_t y_row_stride, int32_t* status, void* stream) {
+  clear_error();
+  GDN_REQUIRE(n_seqs >= 0 && n_tokens >= 0 && channels > 0,
+              "gdn_causal_conv_silu_varlen: bad sizes (n_seqs=%d, n_tokens=%lld, channels=%d)",
+              n_seqs, (long long)n_tokens, channels);
+  GDN_UNSUPPORTED(kernel >= 2 && kernel <= 4,
+                  "gdn_causal_conv_silu_varlen: kernel %d unsupported (2..4)", kernel);
+  GDN_REQUIRE(x_row_stride >= channels && y_row_stride >= channels,
+              "gdn_causal_conv_silu_varlen: row stride smaller than channels");
+  GDN_REQUIRE(num_slots > 0 && slot_stride >= (int64_t)channels * (kernel - 1),
+              "gdn_causal_conv_silu_varlen: slot_stride too small");
+  GDN_REQUIRE(n_seqs > 0 || n_tokens == 0, "gdn_causal_conv_silu_varlen: tokens without sequences");
+  if (n_seqs == 0) return GDN_OK;
+  GDN_REQUIRE(x && conv_pool && ids && cu_seqlens && weight && y,
+              "gdn_causal_conv_silu_varlen: null pointer");
+  const bool vec = channels % 8 == 0 && x_row_stride % 8 == 0 && y_row_stride % 8 == 0 &&
+                   aligned16(x) && aligned16(y) && aligned16(weight);
+  cudaStream_t s = (cudaStream_t)stream;
+  const int per_cta = vec ? kConvThreads * 8 : kConvThreads;
+  const int64_t tiles = (n_tokens + kConvTileTokens - 1) / kConvTileTokens;
+  GDN_UNSUPPORTED(tiles < (1ll << 31), "gdn_causal_conv_silu_varlen: too many tokens");
+  dim3 wgrid((channels + kConvThreads - 1) / kConvThreads, n_seqs);
+#define GDN_VL(KK)                                                                               \
+  if (kernel == KK) {                                                                            \
+    if (tiles > 0) {                                                                             \
+      dim3 grid((unsigned)tiles, (channels + per_cta - 1) / per_cta);                            \
+      if (vec)                                                                                   \
+        conv_varlen_kernel<KK, true><<<grid, kConvThreads, 0, s>>>(                              \
+            (const bf16*)x, x_row_stride, (const bf16*)conv_pool, slot_stride, num_slots, ids,   \
+            cu_seqlens, n_seqs, n_tokens, channels, (const bf16*)weight, (bf16*)y, y_row_stride, \
+            status);                                                                             \
+      else                                                                                       \
+        conv_varlen_kernel<KK, false><<<grid, kConvThreads, 0, s>>>(                             \
+            (const bf16*)x, x_row_stride, (const bf16*)conv_pool, slot_stride, num_slots, ids,   \
+            cu_seqlens, n_seqs, n_tokens, channels, (const bf16*)weight, (bf16*)y, y_row_stride, \
+            status);                                                                             \
+    }                                                                                            \
+    conv_state_writeback_kernel<KK><<<wgrid, kConvThreads, 0, s>>>(                              \
+        (const bf16*)x, x_row_stride, (bf16*)conv_pool, slot_stride, num_slots, ids, cu_seqlens, \
+        channels, n_tokens);                                                                            \
+  }
+  GDN_VL(2) GDN_VL(3) GDN_VL(4)
+#undef GDN_VL
+  return check_launch("gdn_causal_conv_silu_varlen");
+}

@@ -1,0 +1,139 @@
+// (b) fused g/beta gate and the gated RMSNorm epilogue.
+//
+// Both are HBM-bound elementwise / row kernels.  The gate reads 2+2 bytes
+// and writes 4+2 bytes per (token, v-head); the norm reads x and gate and
+// writes y (6 bytes per element).  Grids are sized to a multiple of the SM
+// count with grid-stride loops.
+#include "common.cuh"
+
+namespace gdn {
+
+template <typename P>
+__device__ __forceinline__ float load_param(const P* p, int i);
+template <>
+__device__ __forceinline__ float load_param<float>(const float* p, int i) { return p[i]; }
+template <>
+__device__ __forceinline__ float load_param<bf16>(const bf16* p, int i) { return bf2f(p[i]); }
+
+// g = -exp(A_log) * softplus(a + dt_bias) (threshold 20), beta = sigmoid(b).
+// Follows qwen3_5.py:320-343 step for step (fp32 arithmetic).
+template <typename P>
+__global__ void __launch_bounds__(256) gbeta_kernel(
+    const bf16* __restrict__ b, const bf16* __restrict__ a, int64_t row_stride,
+    int64_t n_rows, int H, const P* __restrict__ a_log, const P* __restrict__ dt_bias,
+    const uint8_t* __restrict__ mask, float* __restrict__ g, bf16* __restrict__ beta) {
+  const int64_t total = n_rows * H;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t r = i / H;
+    const int h = (int)(i - r * H);
+    const float av = bf2f(a[r * row_stride + h]);
+    const float bv = bf2f(b[r * row_stride + h]);
+    const float z = av + load_param<P>(dt_bias, h);
+    const float sp = z > 20.0f ? z : logf(1.0f + expf(z));
+    float gv = -expf(load_param<P>(a_log, h)) * sp;
+    if (mask != nullptr && mask[r] == 0) gv = 0.0f;
+    g[i] = gv;
+    beta[i] = f2bf(sigmoidf_(bv));
+  }
+}
+
+// One warp per row: y = bf16(bf16(w * bf16(x * rsqrt(mean x^2 + eps))) * silu(gate)),
+// the rounding sequence of qwen3_5.py:121-131 for a bf16 model.
+template <int DIM>
+__global__ void __launch_bounds__(256) rms_gated_kernel(
+    const bf16* __restrict__ x, const bf16* __restrict__ gate, int64_t gate_token_stride,
+    int heads, const bf16* __restrict__ w, bf16* __restrict__ y, int64_t n_rows, float eps) {
+  constexpr int PER = DIM / 32;
+  const int lane = threadIdx.x & 31;
+  const int64_t warps_total = (int64_t)gridDim.x * (blockDim.x >> 5);
+  for (int64_t row = blockIdx.x * (int64_t)(blockDim.x >> 5) + (threadIdx.x >> 5); row < n_rows;
+       row += warps_total) {
+    float xv[PER];
+    float ss = 0.f;
+#pragma unroll
+    for (int i = 0; i < PER; ++i) {
+      xv[i] = bf2f(x[row * DIM + lane + 32 * i]);
+      ss += xv[i] * xv[i];
+    }
+    ss = warp_sum(ss);
+    const float inv = rsqrtf(ss / (float)DIM + eps);
+    const int64_t tok = row / heads;
+    const bf16* grow = gate + tok * gate_token_stride + (row - tok * heads) * DIM;
+#pragma unroll
+    for (int i = 0; i < PER; ++i) {
+      const int c = lane + 32 * i;
+      const float t = round_bf(xv[i] * inv);
+      const float u = round_bf(bf2f(w[c]) * t);
+      const float gz = bf2f(grow[c]);
+      y[row * DIM + c] = f2bf(u * siluf_(gz));
+    }
+  }
+}
+
+}  // namespace gdn
+
+using namespace gdn;
+
+extern "C" int gdn_fused_g_beta(const void* b, const void* a, int64_t ab_row_stride,
+                                int64_t n_rows, int32_t num_v_heads, const void* a_log,
+                                const void* dt_bias, int32_t param_dtype,
+                                const uint8_t* row_mask, float* g, void* beta, void* stream) {
+  clear_error();
+  GDN_REQUIRE(n_rows >= 0 && num_v_heads > 0, "gdn_fused_g_beta: bad sizes (n_rows=%lld, heads=%d)",
+              (long long)n_rows, num_v_heads);
+  GDN_REQUIRE(ab_row_stride >= num_v_heads, "gdn_fused_g_beta: row stride %lld < heads %d",
+              (long long)ab_row_stride, num_v_heads);
+  GDN_REQUIRE(param_dtype == GDN_DTYPE_F32 || param_dtype == GDN_DTYPE_BF16,
+              "gdn_fused_g_beta: param_dtype must be F32 or BF16");
+  if (n_rows == 0) return GDN_OK;
+  GDN_REQUIRE(b && a && a_log && dt_bias && g && beta, "gdn_fused_g_beta: null pointer");
+  const int64_t total = n_rows * num_v_heads;
+  int64_t blocks = (total + 255) / 256;
+  const int64_t cap = (int64_t)sm_count() * 8;
+  if (blocks > cap) blocks = cap;
+  cudaStream_t s = (cudaStream_t)stream;
+  if (param_dtype == GDN_DTYPE_F32)
+    gbeta_kernel<float><<<(unsigned)blocks, 256, 0, s>>>(
+        (const bf16*)b, (const bf16*)a, ab_row_stride, n_rows, num_v_heads, (const float*)a_log,
+        (const float*)dt_bias, row_mask, g, (bf16*)beta);
+  else
+    gbeta_kernel<bf16><<<(unsigned)blocks, 256, 0, s>>>(
+        (const bf16*)b, (const bf16*)a, ab_row_stride, n_rows, num_v_heads, (const bf16*)a_log,
+        (const bf16*)dt_bias, row_mask, g, (bf16*)beta);
+  return check_launch("gdn_fused_g_beta");
+}
+
+extern "C" int gdn_rms_norm_gated(const void* x, const void* gate, int64_t gate_token_stride,
+                                  int32_t heads_per_token, const void* weight, void* y,
+                                  int64_t n_rows, int32_t dim, float eps, void* stream) {
+  clear_error();
+  GDN_REQUIRE(n_rows >= 0, "gdn_rms_norm_gated: n_rows < 0");
+  GDN_UNSUPPORTED(dim == 64 || dim == 128 || dim == 256,
+                  "gdn_rms_norm_gated: dim %d unsupported (64, 128, 256)", dim);
+  GDN_REQUIRE(heads_per_token > 0 && n_rows % heads_per_token == 0,
+              "gdn_rms_norm_gated: n_rows %lld not a multiple of heads_per_token %d",
+              (long long)n_rows, heads_per_token);
+  GDN_REQUIRE(gate_token_stride >= (int64_t)heads_per_token * dim,
+              "gdn_rms_norm_gated: gate token stride < heads_per_token * dim");
+  if (n_rows == 0) return GDN_OK;
+  GDN_REQUIRE(x && gate && weight && y, "gdn_rms_norm_gated: null pointer");
+  int64_t blocks = (n_rows + 7) / 8;
+  const int64_t cap = (int64_t)sm_count() * 16;
+  if (blocks > cap) blocks = cap;
+  cudaStream_t s = (cudaStream_t)stream;
+#define GDN_NORM_CASE(D)                                                                      \
+  case D:                                                                                     \
+    rms_gated_kernel<D><<<(unsigned)blocks, 256, 0, s>>>((const bf16*)x, (const bf16*)gate,  \
+                                                         gate_token_stride, heads_per_token,  \
+                                                         (const bf16*)weight,                 \
+                                                         (bf16*)y, n_rows, eps);              \
+    break;
+  switch (dim) {
+    GDN_NORM_CASE(64)
+    GDN_NORM_CASE(128)
+    GDN_NORM_CASE(256)
+  }
+#undef GDN_NORM_CASE
+  return check_launch("gdn_rms_norm_gated");
+}

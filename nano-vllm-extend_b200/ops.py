@@ -1,0 +1,284 @@
+"""Tensor-level GDN operators over the C ABI (libgdn_b200.so).
+
+Each function keeps the name and argument meaning of the reference operator it
+replaces (sileaver/nano-vllm-extend, nanovllm/models/qwen3_5.py) and raises on
+the same contract violations (``AssertionError`` for the layout asserts the
+reference makes, ``ValueError`` / ``NotImplementedError`` for what the library
+rejects).  Kernels launch on the current CUDA stream and never synchronise, so
+every operator is CUDA-graph capturable.  Where the reference gathers and
+scatters pool rows around a kernel, these operators take the pool view and the
+slot ids and update the slots in place.
+
+Slot-id faults never touch memory: the kernels skip such rows and raise a bit
+in a per-device status word; :func:`check_status` reads and clears it (it
+synchronises, so call it in tests and debug paths, not every step).
+"""
+from __future__ import annotations
+
+import torch
+
+from . import _lib
+
+_STATUS: dict[int, torch.Tensor] = {}
+
+
+def _stream_ptr(device: torch.device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def status_word(device) -> torch.Tensor:
+    """The int32 device status word the kernels OR fault bits into."""
+    device = torch.device(device)
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    t = _STATUS.get(idx)
+    if t is None:
+        t = torch.zeros(1, dtype=torch.int32, device=torch.device("cuda", idx))
+        _STATUS[idx] = t
+    return t
+
+
+def check_status(device=None, clear: bool = True) -> int:
+    """Read (and clear) the status word; raise if a kernel flagged a fault."""
+    device = device if device is not None else torch.device("cuda", torch.cuda.current_device())
+    st = status_word(device)
+    v = int(st.item())
+    if clear:
+        st.zero_()
+    if v & _lib.GDN_STATUS_BAD_SLOT:
+        raise IndexError(f"GDN kernel saw a slot id outside the pool (status {v:#x})")
+    if v & _lib.GDN_STATUS_BAD_SEQLEN:
+        raise ValueError(f"GDN kernel saw malformed cu_seqlens / max_seqlen (status {v:#x})")
+    return v
+
+
+def _p(t) -> int:
+    return 0 if t is None else t.data_ptr()
+
+
+def _cuda(*ts):
+    for t in ts:
+        if t is not None:
+            assert t.is_cuda, "GDN operators take CUDA tensors"
+
+
+def _ids64(ids: torch.Tensor) -> torch.Tensor:
+    assert ids.dim() == 1, "linear_state_ids must be 1-D"
+    if ids.dtype != torch.int64 or not ids.is_contiguous():
+        ids = ids.to(torch.int64).contiguous()
+    return ids
+
+
+def _rows2d(x: torch.Tensor, width: int) -> tuple[torch.Tensor, int]:
+    """View x as [rows, width] rows with a row stride (last dim dense)."""
+    x2 = x.reshape(-1, width) if x.is_contiguous() else x
+    if x2.dim() != 2:
+        x2 = x.reshape(-1, width)
+    assert x2.stride(-1) == 1, "last dimension must be dense"
+    return x2, x2.stride(0)
+
+
+# ---------------------------------------------------------------------------
+# (b) gate
+# ---------------------------------------------------------------------------
+
+
+def fused_g_beta(b: torch.Tensor, a: torch.Tensor, a_log: torch.Tensor,
+                 dt_bias: torch.Tensor, mask: torch.Tensor | None = None):
+    """qwen3_5.py:346-360.  b/a [.., Vh] bf16 (rows may be strided views);
+    a_log/dt_bias [Vh]; mask [..] bool or None (False rows get g = 0).
+    Returns (g fp32 [.., Vh], beta bf16 [.., Vh]), both contiguous."""
+    _cuda(b, a, a_log, dt_bias, mask)
+    assert b.dtype == torch.bfloat16 and a.dtype == torch.bfloat16
+    assert a.shape == b.shape
+    vh = a.shape[-1]
+    assert a_log.numel() == vh and dt_bias.numel() == vh
+    lead = a.shape[:-1]
+    if a.dim() != 2 or b.dim() != 2 or a.stride(0) != b.stride(0) or a.stride(1) != 1 \
+            or b.stride(1) != 1:
+        a = a.reshape(-1, vh).contiguous()
+        b = b.reshape(-1, vh).contiguous()
+    n = a.shape[0]
+    assert a_log.dtype == dt_bias.dtype
+    pdt = _lib.GDN_DTYPE_BF16 if a_log.dtype == torch.bfloat16 else _lib.GDN_DTYPE_F32
+    if pdt == _lib.GDN_DTYPE_F32:
+        a_log, dt_bias = a_log.float().contiguous(), dt_bias.float().contiguous()
+    else:
+        a_log, dt_bias = a_log.contiguous(), dt_bias.contiguous()
+    g = torch.empty(*lead, vh, dtype=torch.float32, device=a.device)
+    beta = torch.empty(*lead, vh, dtype=torch.bfloat16, device=a.device)
+    m = None
+    if mask is not None:
+        m = mask.reshape(-1).to(torch.uint8).contiguous()
+        assert m.numel() == n
+    rc = _lib.load().gdn_fused_g_beta(
+        _p(b), _p(a), a.stride(0), n, vh, _p(a_log), _p(dt_bias), pdt, _p(m), _p(g), _p(beta),
+        _stream_ptr(a.device))
+    _lib.check(rc, "gdn_fused_g_beta")
+    return g, beta
+
+
+# ---------------------------------------------------------------------------
+# (a) conv
+# ---------------------------------------------------------------------------
+
+
+def _pool_view_check(pool: torch.Tensor, taps: int, channels: int):
+    assert pool.dim() == 3 and pool.shape[1] == channels and pool.shape[2] == taps, \
+        f"conv pool view must be [slots, {channels}, {taps}]"
+    assert pool.stride(2) == 1 and pool.stride(1) == taps, "conv pool taps must be dense"
+    assert pool.dtype == torch.bfloat16
+
+
+def conv_decode_step(x: torch.Tensor, state_pool: torch.Tensor, ids: torch.Tensor,
+                     weight: torch.Tensor) -> torch.Tensor:
+    """qwen3_5.py:550-558.  x [n, C] (rows may be strided); state_pool
+    [slots, C, K-1] rolled in place at rows ``ids``; weight [C, K] (or the
+    conv1d weight [C, 1, K]).  Returns y [n, C]."""
+    _cuda(x, state_pool, ids, weight)
+    C = x.shape[-1]
+    w = weight.reshape(C, -1).contiguous()
+    K = w.shape[1]
+    _pool_view_check(state_pool, K - 1, C)
+    assert x.dtype == torch.bfloat16 and w.dtype == torch.bfloat16
+    x2, xs = _rows2d(x, C)
+    n = x2.shape[0]
+    ids = _ids64(ids)
+    assert ids.numel() == n
+    y = torch.empty(n, C, dtype=x.dtype, device=x.device)
+    rc = _lib.load().gdn_conv_decode_step(
+        _p(x2), xs, _p(state_pool), state_pool.stride(0), state_pool.shape[0], _p(ids), n, C, K,
+        _p(w), _p(y), y.stride(0), _p(status_word(x.device)), _stream_ptr(x.device))
+    _lib.check(rc, "gdn_conv_decode_step")
+    return y
+
+
+def causal_conv_silu_varlen(x: torch.Tensor, state_pool: torch.Tensor, ids: torch.Tensor,
+                            weight: torch.Tensor, cu_seqlens: torch.Tensor) -> torch.Tensor:
+    """Varlen causal conv + SiLU (qwen3_5.py:459-473), with each sequence's
+    prefix state read from and rolled in place in ``state_pool[ids[r]]``
+    (the gather/scatter of qwen3_5.py:941-946 is not needed).  x [N, C];
+    cu_seqlens int32 [n+1] on the device.  Returns y [N, C] (the reference's
+    [3, N, C/3] slabs are its own layout; q/k/v are column views of y here)."""
+    _cuda(x, state_pool, ids, weight, cu_seqlens)
+    C = x.shape[-1]
+    w = weight.reshape(C, -1).contiguous()
+    K = w.shape[1]
+    _pool_view_check(state_pool, K - 1, C)
+    x2, xs = _rows2d(x, C)
+    N = x2.shape[0]
+    ids = _ids64(ids)
+    cu = cu_seqlens.to(torch.int32).contiguous() if cu_seqlens.dtype != torch.int32 \
+        else cu_seqlens.contiguous()
+    assert cu.numel() == ids.numel() + 1, "cu_seqlens must have n_seqs + 1 entries"
+    y = torch.empty(N, C, dtype=x.dtype, device=x.device)
+    rc = _lib.load().gdn_causal_conv_silu_varlen(
+        _p(x2), xs, _p(state_pool), state_pool.stride(0), state_pool.shape[0], _p(ids), _p(cu),
+        ids.numel(), N, C, K, _p(w), _p(y), y.stride(0), _p(status_word(x.device)),
+        _stream_ptr(x.device))
+    _lib.check(rc, "gdn_causal_conv_silu_varlen")
+    return y
+
+
+# ---------------------------------------------------------------------------
+# (d) recurrent decode, (c) chunk prefill
+# ---------------------------------------------------------------------------
+
+
+def _heads(t: torch.Tensor, name: str):
+    """[rows, (1,) H, D] view -> (rows, H, D, row_stride); heads dense."""
+    if t.dim() == 4:
+        assert t.shape[1] == 1, f"{name}: expected [bs, 1, H, D]"
+        t = t[:, 0]
+    assert t.dim() == 3, f"{name}: expected [rows, H, D]"
+    rows, H, D = t.shape
+    assert t.stride(2) == 1 and (H == 1 or t.stride(1) == D), \
+        f"{name}: heads must be dense within a row (stride(2) == {D})"
+    return rows, H, D, t.stride(0)
+
+
+def _state_view_check(s_pool: torch.Tensor, HV: int, DK: int, DV: int):
+    assert s_pool.dim() == 4 and tuple(s_pool.shape[1:]) == (HV, DK, DV), \
+        f"state pool view must be [slots, {HV}, {DK}, {DV}]"
+    assert s_pool.dtype == torch.float32
+    assert s_pool.stride(1) == DK * DV and s_pool.stride(2) == DV and s_pool.stride(3) == 1
+
+
+def recurrent_gdn_inplace(q, k, v, g, beta, s_pool, ids) -> torch.Tensor:
+    """qwen3_5.py:596-613.  q/k [bs, 1, HK, DK] (or HK == HV, already
+    repeated), v [bs, 1, HV, DV] — strided row views allowed; g fp32 /
+    beta bf16 [bs, 1, HV]; s_pool [slots, HV, DK, DV] fp32 per-layer view,
+    rows ``ids`` updated in place.  Returns out [bs, 1, HV, DV] bf16."""
+    _cuda(q, k, v, g, beta, s_pool, ids)
+    bs, HK, DK, qs = _heads(q, "q")
+    bs_k, HK_k, DK_k, ks = _heads(k, "k")
+    bs_v, HV, DV, vs = _heads(v, "v")
+    assert bs_k == bs and bs_v == bs and HK_k == HK and DK_k == DK
+    assert HV % HK == 0
+    g = g.reshape(bs, HV)
+    beta = beta.reshape(bs, HV)
+    assert g.dtype == torch.float32 and g.is_contiguous() and beta.is_contiguous(), \
+        "g / beta must be contiguous"
+    _state_view_check(s_pool, HV, DK, DV)
+    ids = _ids64(ids)
+    assert ids.numel() == bs
+    out = torch.empty(bs, 1, HV, DV, dtype=v.dtype, device=v.device)
+    rc = _lib.load().gdn_recurrent_inplace(
+        _p(q), qs, _p(k), ks, _p(v), vs, _p(g), _p(beta), _p(s_pool), s_pool.stride(0),
+        s_pool.shape[0], _p(ids), _p(out), bs, HK, HV, DK, DV, DK ** -0.5,
+        _p(status_word(v.device)), _stream_ptr(v.device))
+    _lib.check(rc, "gdn_recurrent_inplace")
+    return out
+
+
+def chunk_gated_delta_rule_varlen(q, k, v, g, beta, s_pool, ids, cu_seqlens,
+                                  max_seqlen: int) -> torch.Tensor:
+    """Varlen chunked prefill (the chunk rule of qwen3_5.py:140-227 driven by
+    cu_seqlens as at :956-961), initial state read from and final state
+    written to ``s_pool[ids[r]]``.  q/k [N, HK, DK], v [N, HV, DV] (row
+    views allowed), g fp32 / beta bf16 [N, HV].  Returns out [N, HV, DV]."""
+    _cuda(q, k, v, g, beta, s_pool, ids, cu_seqlens)
+    N, HK, DK, qs = _heads(q, "q")
+    N_k, HK_k, DK_k, ks = _heads(k, "k")
+    N_v, HV, DV, vs = _heads(v, "v")
+    assert N_k == N and N_v == N and HK_k == HK and DK_k == DK and HV % HK == 0
+    g = g.reshape(N, HV)
+    beta = beta.reshape(N, HV)
+    assert g.dtype == torch.float32 and g.is_contiguous() and beta.is_contiguous()
+    _state_view_check(s_pool, HV, DK, DV)
+    ids = _ids64(ids)
+    cu = cu_seqlens.to(torch.int32).contiguous() if cu_seqlens.dtype != torch.int32 \
+        else cu_seqlens.contiguous()
+    assert cu.numel() == ids.numel() + 1
+    out = torch.empty(N, HV, DV, dtype=v.dtype, device=v.device)
+    rc = _lib.load().gdn_chunk_prefill_varlen(
+        _p(q), qs, _p(k), ks, _p(v), vs, _p(g), _p(beta), _p(s_pool), s_pool.stride(0),
+        s_pool.shape[0], _p(ids), _p(cu), ids.numel(), N, int(max_seqlen), _p(out), HK, HV, DK,
+        DV, DK ** -0.5, _p(status_word(v.device)), _stream_ptr(v.device))
+    _lib.check(rc, "gdn_chunk_prefill_varlen")
+    return out
+
+
+def rms_norm_gated(x: torch.Tensor, gate: torch.Tensor, weight: torch.Tensor,
+                   eps: float) -> torch.Tensor:
+    """qwen3_5.py:121-131 (Qwen3_5RMSNormGated.forward).  x [.., D] bf16,
+    gate with x's shape; for a [tokens, heads, D] gate the token stride may
+    exceed heads*D (a column slice of a fused projection).  weight [D].
+    Returns y with x's shape."""
+    _cuda(x, gate, weight)
+    D = x.shape[-1]
+    assert x.dtype == torch.bfloat16 and gate.dtype == torch.bfloat16 and \
+        weight.dtype == torch.bfloat16
+    assert gate.shape == x.shape
+    x = x.contiguous()
+    n = x.numel() // D
+    if gate.dim() == 3 and gate.stride(2) == 1 and (gate.shape[1] == 1 or gate.stride(1) == D):
+        g3 = gate
+    else:
+        g3 = gate.reshape(-1, 1, D).contiguous() if gate.dim() != 3 else gate.contiguous()
+    heads = g3.shape[1]
+    y = torch.empty_like(x)
+    rc = _lib.load().gdn_rms_norm_gated(
+        _p(x), _p(g3), g3.stride(0), heads, _p(weight.contiguous()), _p(y), n, D, float(eps),
+        _stream_ptr(x.device))
+    _lib.check(rc, "gdn_rms_norm_gated")
+    return y

@@ -1,0 +1,335 @@
+"""GPU parity of each GDN kernel (through the C ABI) against the CPU oracle
+and the reference's golden vectors.
+
+Tolerances (from the path's spec): bf16 outputs max-abs <= 2e-2; fp32 states
+relative error <= 1e-3 (Frobenius norm of the difference over the norm of the
+oracle state); slot indexing, untouched slots and sequence boundaries
+bit-exact.  Inputs are bf16-representable, so the oracle and the GPU see
+identical values.
+"""
+import os
+
+import numpy as np
+import pytest
+import torch
+
+import inputs as I
+from oracle import gdn_oracle as O
+
+pytestmark = pytest.mark.gpu
+
+OUT_ATOL = 2e-2
+STATE_RTOL = 1e-3
+
+
+@pytest.fixture(scope="module")
+def ops(pkg):
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    torch.cuda.set_device(0)
+    return pkg.ops
+
+
+DEV = "cuda:0"
+
+
+def bf(a):
+    return torch.from_numpy(np.ascontiguousarray(a, np.float32)).to(DEV).to(torch.bfloat16)
+
+
+def f32(a):
+    return torch.from_numpy(np.ascontiguousarray(a, np.float32)).to(DEV)
+
+
+def i64(a):
+    return torch.from_numpy(np.ascontiguousarray(a, np.int64)).to(DEV)
+
+
+def i32(a):
+    return torch.from_numpy(np.ascontiguousarray(a, np.int32)).to(DEV)
+
+
+def host(t):
+    return t.float().cpu().numpy()
+
+
+def bf16_ulp(x):
+    ax = np.maximum(np.abs(x), 1e-30)
+    return 2.0 ** (np.floor(np.log2(ax)) - 7)
+
+
+def assert_bf16_close(a, b, ulps=1, atol=1e-6):
+    a = np.asarray(a, np.float32); b = np.asarray(b, np.float32)
+    tol = ulps * bf16_ulp(np.maximum(np.abs(a), np.abs(b))) + atol
+    bad = np.abs(a - b) > tol
+    assert not bad.any(), f"{bad.sum()}/{bad.size} differ, max |d| {np.abs(a - b).max()}"
+
+
+def state_rel(a, b):
+    return float(np.linalg.norm(a - b) / max(np.linalg.norm(b), 1e-30))
+
+
+def load(golden_dir, name):
+    return dict(np.load(os.path.join(golden_dir, name)))
+
+
+# ---------------------------------------------------------------------------
+# (b) gate
+# ---------------------------------------------------------------------------
+
+
+def test_gbeta_golden(ops, golden_dir):
+    d = load(golden_dir, "gbeta.npz")
+    for mask, gk, bk in ((d["mask"], "g_mask", "beta_mask"), (None, "g", "beta")):
+        m = None if mask is None else torch.from_numpy(mask).to(DEV)
+        g, beta = ops.fused_g_beta(bf(d["b"]), bf(d["a"]), bf(d["a_log"]), bf(d["dt_bias"]), m)
+        np.testing.assert_allclose(host(g), d[gk], rtol=2e-6, atol=1e-6)
+        assert_bf16_close(host(beta), d[bk])
+    # fp32 parameters and strided row views
+    big = bf(np.concatenate([d["b"].reshape(15, 8), d["a"].reshape(15, 8)], 1))
+    g, beta = ops.fused_g_beta(big[:, :8], big[:, 8:], f32(d["a_log"]), f32(d["dt_bias"]))
+    np.testing.assert_allclose(host(g), d["g"].reshape(15, 8), rtol=2e-6, atol=1e-6)
+
+
+# ---------------------------------------------------------------------------
+# (a) conv
+# ---------------------------------------------------------------------------
+
+
+def test_conv_decode_golden(ops, golden_dir):
+    d = load(golden_dir, "conv_decode.npz")
+    pool = bf(d["pool_in"])
+    y = ops.conv_decode_step(bf(d["x"]), pool[:, int(d["layer"])], i64(d["ids"]), bf(d["w"]))
+    assert_bf16_close(host(y), d["y"])
+    assert np.array_equal(host(pool), d["pool_out"])   # roll is bit-exact, other slots untouched
+    ops.check_status()
+
+
+@pytest.mark.parametrize("C", [1024, 96, 100])
+def test_conv_decode_vs_oracle(ops, C):
+    r = I.rng(31)
+    n, K, slots, L = 7, 4, 12, 3
+    x = O.round_bf16(r.standard_normal((n, C + 16)).astype(np.float32))   # strided rows
+    pool = O.round_bf16(r.standard_normal((slots, L, C, K - 1)).astype(np.float32))
+    w = O.round_bf16(r.uniform(-0.6, 0.6, (C, K)).astype(np.float32))
+    ids = r.permutation(slots)[:n]
+    pool_d = bf(pool)
+    y = ops.conv_decode_step(bf(x)[:, :C], pool_d[:, 2], i64(ids), bf(w))
+    ref_pool = pool.copy()
+    ref = O.conv_decode_step(x[:, :C], ref_pool[:, 2], ids, w)
+    assert_bf16_close(host(y), ref)
+    assert np.array_equal(host(pool_d), ref_pool)
+
+
+@pytest.mark.parametrize("C", [1024, 96, 100])
+def test_conv_varlen_vs_oracle(ops, C):
+    r = I.rng(32)
+    lens = [0, 1, 2, 3, 31, 32, 33, 100, 0, 5]
+    N = sum(lens)
+    K, slots, L = 4, 14, 2
+    x = O.round_bf16(r.standard_normal((N, C)).astype(np.float32))
+    pool = O.round_bf16(r.standard_normal((slots, L, C, K - 1)).astype(np.float32))
+    w = O.round_bf16(r.uniform(-0.6, 0.6, (C, K)).astype(np.float32))
+    ids = r.permutation(slots)[:len(lens)]
+    cu = I.cu_from_lens(lens)
+    pool_d = bf(pool)
+    y = ops.causal_conv_silu_varlen(bf(x), pool_d[:, 1], i64(ids), bf(w), i32(cu))
+    ref_pool = pool.copy()
+    ref = O.causal_conv_silu_varlen(x, ref_pool[:, 1], ids, cu, w)
+    assert_bf16_close(host(y), ref)
+    # sequence boundaries and the state roll are bit-exact; empty sequences
+    # and every other slot / layer are untouched
+    assert np.array_equal(host(pool_d), ref_pool)
+    ops.check_status()
+
+
+def test_conv_padded_golden_rows(ops, golden_dir):
+    """Rows of the reference's padded conv whose writeback is at T match the
+    varlen kernel (values and state)."""
+    d = load(golden_dir, "conv_padded.npz")
+    T = d["x"].shape[2]
+    for row in [r for r in range(d["x"].shape[0]) if d["endp"][r] == T]:
+        pool = bf(d["state_in"][row][None])
+        y = ops.causal_conv_silu_varlen(bf(d["x"][row].T), pool, i64([0]), bf(d["w"]),
+                                        i32([0, T]))
+        assert_bf16_close(host(y).T, d["y"][row])
+        assert np.array_equal(host(pool)[0], d["state_out"][row])
+
+
+def test_conv_split_equals_one_shot(ops):
+    """Chunked prefill continuation: two calls over a split sequence equal one
+    call (the conv state threads across calls)."""
+    r = I.rng(33)
+    C, K = 512, 4
+    x = O.round_bf16(r.standard_normal((150, C)).astype(np.float32))
+    w = O.round_bf16(r.uniform(-0.6, 0.6, (C, K)).astype(np.float32))
+    p1 = torch.zeros(2, C, K - 1, dtype=torch.bfloat16, device=DEV)
+    p2 = p1.clone()
+    y1 = ops.causal_conv_silu_varlen(bf(x), p1, i64([1]), bf(w), i32([0, 150]))
+    ya = ops.causal_conv_silu_varlen(bf(x[:61]), p2, i64([1]), bf(w), i32([0, 61]))
+    yb = ops.causal_conv_silu_varlen(bf(x[61:62]), p2, i64([1]), bf(w), i32([0, 1]))
+    yc = ops.causal_conv_silu_varlen(bf(x[62:]), p2, i64([1]), bf(w), i32([0, 88]))
+    assert torch.equal(y1, torch.cat([ya, yb, yc]))
+    assert torch.equal(p1, p2)
+
+
+# ---------------------------------------------------------------------------
+# (d) recurrent decode
+# ---------------------------------------------------------------------------
+
+
+def test_recurrent_golden(ops, golden_dir):
+    d = load(golden_dir, "recurrent_inplace.npz")
+    HK, HV, D = int(d["HK"]), int(d["HV"]), int(d["D"])
+    slots, L, bs = 9, 2, 5
+    pool = I.recurrent_pool(slots, L, HV, D)
+    layer = int(d["layer"])
+    pool_d = f32(pool)
+    kd = HK * D
+    for s in range(3):
+        mixed, g, beta = I.recurrent_step_inputs(bs, HK, HV, D, s)
+        m = bf(mixed)
+        q = m[:, :kd].view(bs, 1, HK, D)
+        k = m[:, kd:2 * kd].view(bs, 1, HK, D)
+        v = m[:, 2 * kd:].view(bs, 1, HV, D)
+        out = ops.recurrent_gdn_inplace(q, k, v, f32(g).view(bs, 1, HV), bf(beta).view(bs, 1, HV),
+                                        pool_d[:, layer], i64(d["ids"]))
+        assert np.abs(host(out)[:, 0] - d[f"out{s}"]).max() <= OUT_ATOL
+        assert_bf16_close(host(out)[:, 0], d[f"out{s}"], ulps=2, atol=1e-4)
+    got = host(pool_d)
+    assert state_rel(got[d["ids"], layer], d["rows_out"]) <= 1e-5
+    untouched = np.setdiff1d(np.arange(slots), d["ids"])
+    assert np.array_equal(got[untouched], pool[untouched])
+    assert np.array_equal(got[:, 0], pool[:, 0])
+
+
+@pytest.mark.parametrize("bs", [64, 2])   # full-tile and column-split launches
+def test_recurrent_d128_vs_oracle(ops, bs):
+    HK, HV, D, slots, L = 16, 32, 128, 97, 2
+    r = I.rng(40 + bs)
+    q, k, v, g, beta = I.core_inputs(bs, HK, D, HV, D, seed=41 + bs)
+    q, k, v, beta = (O.round_bf16(t) for t in (q, k, v, beta))
+    pool = (r.standard_normal((slots, L, HV, D, D)) * 0.02).astype(np.float32)
+    ids = r.permutation(slots - 1)[:bs]
+    pool_d = f32(pool)
+    out = ops.recurrent_gdn_inplace(bf(q), bf(k), bf(v), f32(g), bf(beta), pool_d[:, 1], i64(ids))
+    ref_pool = pool.copy()
+    ref = O.recurrent_inplace(q, k, v, g, beta, ref_pool[:, 1], ids)
+    assert np.abs(host(out)[:, 0] - ref).max() <= OUT_ATOL
+    got = host(pool_d)
+    assert state_rel(got[ids, 1], ref_pool[ids, 1]) <= 1e-5
+    mask = np.ones(slots, bool); mask[ids] = False
+    assert np.array_equal(got[mask], pool[mask])
+    assert np.array_equal(got[:, 0], pool[:, 0])
+
+
+def test_recurrent_bad_slot_is_flagged_not_touched(ops):
+    HK, HV, D, slots = 1, 2, 64, 4
+    q, k, v, g, beta = I.core_inputs(3, HK, D, HV, D, seed=5)
+    pool = (I.rng(6).standard_normal((slots, HV, D, D)) * 0.02).astype(np.float32)
+    pool_d = f32(pool)
+    ops.check_status()
+    ops.recurrent_gdn_inplace(bf(q), bf(k), bf(v), f32(g), bf(beta), pool_d,
+                              i64([1, slots, -1]))
+    with pytest.raises(IndexError):
+        ops.check_status()
+    got = host(pool_d)
+    assert np.array_equal(np.delete(got, 1, 0), np.delete(pool, 1, 0))
+
+
+# ---------------------------------------------------------------------------
+# (c) chunked prefill
+# ---------------------------------------------------------------------------
+
+
+def _chunk_case(ops, lens, HK, HV, D, seed, init_scale=0.02):
+    N = sum(lens)
+    q, k, v, g, beta = I.core_inputs(N, HK, D, HV, D, seed=seed)
+    q, k, v, beta = (O.round_bf16(t) for t in (q, k, v, beta))
+    r = I.rng(seed + 1)
+    slots = len(lens) + 3
+    pool = (r.standard_normal((slots, HV, D, D)) * init_scale).astype(np.float32)
+    ids = r.permutation(slots)[:len(lens)]
+    cu = I.cu_from_lens(lens)
+    pool_d = f32(pool)
+    out = ops.chunk_gated_delta_rule_varlen(bf(q), bf(k), bf(v), f32(g), bf(beta), pool_d,
+                                            i64(ids), i32(cu), max(lens))
+    ref_pool = pool.copy()
+    ref = O.chunk_prefill_varlen(q, k, v, g, beta, ref_pool, ids, cu, dtype=np.float64)
+    got_out, got_pool = host(out), host(pool_d)
+    assert np.abs(got_out - ref).max() <= OUT_ATOL
+    for i, sl in enumerate(ids):
+        if lens[i]:
+            assert state_rel(got_pool[sl], ref_pool[sl]) <= STATE_RTOL, f"slot {sl}"
+    untouched = np.setdiff1d(np.arange(slots), [s for s, n in zip(ids, lens) if n])
+    assert np.array_equal(got_pool[untouched], pool[untouched])
+    ops.check_status()
+    return got_out, got_pool
+
+
+def test_chunk_c0_vs_oracle(ops):
+    c = I.C0
+    _chunk_case(ops, list(c["lens"]), c["HK"], c["HV"], c["DK"], seed=0)
+
+
+def test_chunk_ragged_d128(ops):
+    _chunk_case(ops, [1, 2, 63, 64, 65, 130, 0, 200], 2, 4, 128, seed=7)
+
+
+def test_chunk_split_equals_one_shot(ops):
+    """Two varlen calls over a split sequence (the chunked-prefill budget
+    splitting a prompt) give the one-shot state and outputs."""
+    HK, HV, D = 2, 4, 128
+    q, k, v, g, beta = I.core_inputs(300, HK, D, HV, D, seed=9)
+    q, k, v, beta = (O.round_bf16(t) for t in (q, k, v, beta))
+    p1 = torch.zeros(2, HV, D, D, device=DEV)
+    p2 = p1.clone()
+    o1 = ops.chunk_gated_delta_rule_varlen(bf(q), bf(k), bf(v), f32(g), bf(beta), p1, i64([1]),
+                                           i32([0, 300]), 300)
+    parts = []
+    for a, b in ((0, 100), (100, 300)):
+        parts.append(ops.chunk_gated_delta_rule_varlen(
+            bf(q[a:b]), bf(k[a:b]), bf(v[a:b]), f32(g[a:b]), bf(beta[a:b]), p2, i64([1]),
+            i32([0, b - a]), b - a))
+    assert np.abs(host(o1) - host(torch.cat(parts))).max() <= OUT_ATOL
+    assert state_rel(host(p2), host(p1)) <= STATE_RTOL
+
+
+def test_chunk_then_decode_c0(ops):
+    """Config 0 end to end on the core: prefill, then 16 decode steps."""
+    c = I.C0
+    lens = list(c["lens"])
+    HK, HV, D = c["HK"], c["HV"], c["DK"]
+    N = sum(lens)
+    q, k, v, g, beta = I.core_inputs(N, HK, D, HV, D, seed=0)
+    q, k, v, beta = (O.round_bf16(t) for t in (q, k, v, beta))
+    ids = np.array([5, 1, 3, 0])
+    pool = np.zeros((7, HV, D, D), np.float32)
+    pool_d = f32(pool)
+    ops.chunk_gated_delta_rule_varlen(bf(q), bf(k), bf(v), f32(g), bf(beta), pool_d, i64(ids),
+                                      i32(I.cu_from_lens(lens)), max(lens))
+    O.chunk_prefill_varlen(q, k, v, g, beta, pool, ids, I.cu_from_lens(lens), dtype=np.float64)
+    for s in range(c["n_decode"]):
+        dq, dk, dv, dg, db = I.core_inputs(4, HK, D, HV, D, seed=1000 + s)
+        dq, dk, dv, db = (O.round_bf16(t) for t in (dq, dk, dv, db))
+        o = ops.recurrent_gdn_inplace(bf(dq), bf(dk), bf(dv), f32(dg), bf(db), pool_d, i64(ids))
+        ref = O.recurrent_inplace(dq, dk, dv, dg, db, pool, ids, dtype=np.float64)
+        assert np.abs(host(o)[:, 0] - ref).max() <= OUT_ATOL
+    got = host(pool_d)
+    for sl in ids:
+        assert state_rel(got[sl], pool[sl]) <= STATE_RTOL
+
+
+# ---------------------------------------------------------------------------
+# gated norm
+# ---------------------------------------------------------------------------
+
+
+def test_rms_gated_golden(ops, golden_dir):
+    d = load(golden_dir, "rms_gated.npz")
+    y = ops.rms_norm_gated(bf(d["x"]), bf(d["z"]), bf(d["w"]), 1e-6)
+    assert_bf16_close(host(y), d["y"], ulps=2)
+    # gate as a strided column slice of a wider buffer
+    zz = bf(np.concatenate([d["z"].reshape(6, 512), np.zeros((6, 40), np.float32)], 1))
+    y2 = ops.rms_norm_gated(bf(d["x"]), zz[:, :512].view(6, 8, 64), bf(d["w"]), 1e-6)
+    assert torch.equal(y, y2)
