@@ -50,12 +50,15 @@ CHUNK_FLOPS_PER_TOKEN_HEAD = 180_224   # 4C*Dk + 2C*Dk + 4C*Dv + 6*Dk*Dv at C=64
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--steps", type=int, default=400)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-prefill", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--prefill-steps", type=int, default=3)
+    ap.add_argument("--profile-case", default=None,
+                    choices=["recurrent", "conv_decode", "conv_varlen", "chunk", "gbeta", "norm"],
+                    help="run a small single-kernel case for ncu (3 launches) and exit")
     return ap.parse_args()
 
 
@@ -110,7 +113,7 @@ class Clocks:
             self.f = open(self.path, "w")
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}",
-                 "--format=csv,noheader,nounits", "-lms", "200"], stdout=self.f,
+                 "--format=csv,noheader,nounits", "-lms", "50"], stdout=self.f,
                 stderr=subprocess.DEVNULL)
         except Exception:
             self.proc = None
@@ -456,9 +459,71 @@ def run_reference(args, world, rank):
 # ---------------------------------------------------------------------------
 
 
+def profile_case(pkg, name):
+    """Small cases for `ncu --set full` (a few hundred MB, 3 launches each):
+    inputs exceed L2 (126 MB) so DRAM counters mean something."""
+    ops = pkg.ops
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev).manual_seed(0)
+    bs, HK, HV, D, C = 256, 16, 32, 128, 8192
+    if name == "recurrent":            # 257-slot pool, 1 layer: 540 MB of state
+        pool = torch.randn(bs + 1, HV, D, D, generator=g, device=dev) * 0.02
+        mixed = torch.randn(bs, C, generator=g, device=dev).to(torch.bfloat16)
+        q = mixed[:, :HK * D].view(bs, HK, D)
+        k = mixed[:, HK * D:2 * HK * D].view(bs, HK, D)
+        v = mixed[:, 2 * HK * D:].view(bs, HV, D)
+        gg = -torch.rand(bs, HV, generator=g, device=dev)
+        beta = torch.rand(bs, HV, generator=g, device=dev).to(torch.bfloat16)
+        ids = torch.randperm(bs + 1, generator=torch.Generator().manual_seed(0))[:bs].to(dev)
+        fn = lambda: ops.recurrent_gdn_inplace(q, k, v, gg, beta, pool, ids)
+    elif name == "conv_decode":        # 4096 rows x 8192 channels
+        n = 4096
+        pool = torch.randn(n + 1, C, 3, generator=g, device=dev).to(torch.bfloat16)
+        x = torch.randn(n, C, generator=g, device=dev).to(torch.bfloat16)
+        w = torch.randn(C, 4, generator=g, device=dev).to(torch.bfloat16)
+        ids = torch.arange(n, device=dev)
+        fn = lambda: ops.conv_decode_step(x, pool, ids, w)
+    elif name in ("conv_varlen", "chunk", "gbeta", "norm"):
+        lens = [4096] * 8 + [1000, 3000, 77, 130]
+        N = sum(lens)
+        cu = torch.tensor(np.concatenate([[0], np.cumsum(lens)]), dtype=torch.int32, device=dev)
+        ids = torch.arange(len(lens), device=dev)
+        x = torch.randn(N, C, generator=g, device=dev).to(torch.bfloat16)
+        if name == "conv_varlen":
+            pool = torch.randn(len(lens), C, 3, generator=g, device=dev).to(torch.bfloat16)
+            w = torch.randn(C, 4, generator=g, device=dev).to(torch.bfloat16)
+            fn = lambda: ops.causal_conv_silu_varlen(x, pool, ids, w, cu)
+        elif name == "chunk":
+            pool = torch.zeros(len(lens), HV, D, D, device=dev)
+            q = x[:, :HK * D].view(N, HK, D)
+            k = x[:, HK * D:2 * HK * D].view(N, HK, D)
+            v = x[:, 2 * HK * D:].view(N, HV, D)
+            gg = -torch.rand(N, HV, generator=g, device=dev)
+            beta = torch.rand(N, HV, generator=g, device=dev).to(torch.bfloat16)
+            fn = lambda: ops.chunk_gated_delta_rule_varlen(q, k, v, gg, beta, pool, ids, cu,
+                                                           max(lens))
+        elif name == "gbeta":
+            ab = torch.randn(N * 64, 2 * HV, generator=g, device=dev).to(torch.bfloat16)
+            al = torch.rand(HV, device=dev)
+            fn = lambda: ops.fused_g_beta(ab[:, :HV], ab[:, HV:], al, al)
+        else:
+            o = torch.randn(N, HV, D, generator=g, device=dev).to(torch.bfloat16)
+            z = torch.randn(N, HV, D, generator=g, device=dev).to(torch.bfloat16)
+            w = torch.ones(D, device=dev, dtype=torch.bfloat16)
+            fn = lambda: ops.rms_norm_gated(o, z, w, 1e-6)
+    for _ in range(3):
+        fn()
+    torch.cuda.synchronize()
+    print(f"profile case {name}: 3 launches done")
+
+
 def main():
     args = parse()
     world, rank, local = dist_setup()
+    if args.profile_case:
+        import __graft_entry__
+        profile_case(__graft_entry__.load_package(), args.profile_case)
+        return
     if args.impl == "reference":
         run_reference(args, world, rank)
         if world > 1:

@@ -34,11 +34,12 @@ DEV = "cuda:0"
 
 
 def bf(a):
-    return torch.from_numpy(np.ascontiguousarray(a, np.float32)).to(DEV).to(torch.bfloat16)
+    return torch.from_numpy(np.array(a, np.float32, order="C", copy=True)).to(DEV).to(
+        torch.bfloat16)
 
 
 def f32(a):
-    return torch.from_numpy(np.ascontiguousarray(a, np.float32)).to(DEV)
+    return torch.from_numpy(np.array(a, np.float32, order="C", copy=True)).to(DEV)
 
 
 def i64(a):
