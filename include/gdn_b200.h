@@ -50,6 +50,7 @@ enum gdn_status_code {
 /* Bits OR-ed into the optional device status word by kernels. */
 #define GDN_STATUS_BAD_SLOT 0x1
 #define GDN_STATUS_BAD_SEQLEN 0x2
+#define GDN_STATUS_TIMEOUT 0x4 /* a bounded device-side wait gave up; outputs invalid */
 
 enum gdn_dtype { GDN_DTYPE_F32 = 0, GDN_DTYPE_BF16 = 1 };
 

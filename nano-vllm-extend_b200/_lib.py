@@ -19,6 +19,7 @@ GDN_ERR_UNSUPPORTED = 2
 GDN_ERR_CUDA = 3
 GDN_STATUS_BAD_SLOT = 0x1
 GDN_STATUS_BAD_SEQLEN = 0x2
+GDN_STATUS_TIMEOUT = 0x4
 GDN_DTYPE_F32 = 0
 GDN_DTYPE_BF16 = 1
 

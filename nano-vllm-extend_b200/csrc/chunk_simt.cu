@@ -220,6 +220,15 @@ int chunk_prefill_simt(int n_seqs, int HV, int D, cudaStream_t s, const bf16* q,
                                num_slots, ids, cu, n_tokens, max_seqlen, out, HK, scale, status);
 }
 
+bool chunk_tc_supported(int D, const void* q, int64_t qs, const void* k, int64_t ks,
+                        const void* v, int64_t vs, const void* out, const void* pool,
+                        int64_t slot_stride);
+int chunk_prefill_tc(int n_seqs, int HV, cudaStream_t s, const bf16* q, int64_t qs,
+                     const bf16* k, int64_t ks, const bf16* v, int64_t vs, const float* g,
+                     const bf16* beta, float* pool, int64_t slot_stride, int64_t num_slots,
+                     const int64_t* ids, const int32_t* cu, int64_t n_tokens, int max_seqlen,
+                     bf16* out, int HK, float scale, int32_t* status);
+
 }  // namespace gdn
 
 using namespace gdn;
@@ -252,6 +261,13 @@ extern "C" int gdn_chunk_prefill_varlen(const void* q, int64_t q_row_stride, con
   if (n_seqs == 0 || n_tokens == 0) return GDN_OK;
   GDN_REQUIRE(q && k && v && g && beta && s_pool && ids && cu_seqlens && out,
               "gdn_chunk_prefill_varlen: null pointer");
+  if (chunk_tc_supported(head_k_dim, q, q_row_stride, k, k_row_stride, v, v_row_stride, out,
+                         s_pool, slot_stride))
+    return chunk_prefill_tc(n_seqs, num_v_heads, (cudaStream_t)stream, (const bf16*)q,
+                            q_row_stride, (const bf16*)k, k_row_stride, (const bf16*)v,
+                            v_row_stride, g, (const bf16*)beta, s_pool, slot_stride, num_slots,
+                            ids, cu_seqlens, n_tokens, max_seqlen, (bf16*)out, num_k_heads, scale,
+                            status);
   return chunk_prefill_simt(n_seqs, num_v_heads, head_k_dim, (cudaStream_t)stream, (const bf16*)q,
                             q_row_stride, (const bf16*)k, k_row_stride, (const bf16*)v,
                             v_row_stride, g, (const bf16*)beta, s_pool, slot_stride, num_slots,

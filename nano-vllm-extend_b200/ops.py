@@ -46,6 +46,8 @@ def check_status(device=None, clear: bool = True) -> int:
         st.zero_()
     if v & _lib.GDN_STATUS_BAD_SLOT:
         raise IndexError(f"GDN kernel saw a slot id outside the pool (status {v:#x})")
+    if v & _lib.GDN_STATUS_TIMEOUT:
+        raise _lib.GdnError(f"GDN kernel gave up a bounded device-side wait (status {v:#x})")
     if v & _lib.GDN_STATUS_BAD_SEQLEN:
         raise ValueError(f"GDN kernel saw malformed cu_seqlens / max_seqlen (status {v:#x})")
     return v
@@ -122,6 +124,15 @@ def fused_g_beta(b: torch.Tensor, a: torch.Tensor, a_log: torch.Tensor,
 # ---------------------------------------------------------------------------
 
 
+def _slot_stride(pool: torch.Tensor) -> int:
+    """Distance between consecutive slots; for a one-slot pool the stride of
+    the slot dim is meaningless (torch/numpy may report 0), so use the
+    slot's own size."""
+    if pool.shape[0] > 1:
+        return pool.stride(0)
+    return max(pool.stride(0), pool[0].numel())
+
+
 def _pool_view_check(pool: torch.Tensor, taps: int, channels: int):
     assert pool.dim() == 3 and pool.shape[1] == channels and pool.shape[2] == taps, \
         f"conv pool view must be [slots, {channels}, {taps}]"
@@ -146,7 +157,7 @@ def conv_decode_step(x: torch.Tensor, state_pool: torch.Tensor, ids: torch.Tenso
     assert ids.numel() == n
     y = torch.empty(n, C, dtype=x.dtype, device=x.device)
     rc = _lib.load().gdn_conv_decode_step(
-        _p(x2), xs, _p(state_pool), state_pool.stride(0), state_pool.shape[0], _p(ids), n, C, K,
+        _p(x2), xs, _p(state_pool), _slot_stride(state_pool), state_pool.shape[0], _p(ids), n, C, K,
         _p(w), _p(y), y.stride(0), _p(status_word(x.device)), _stream_ptr(x.device))
     _lib.check(rc, "gdn_conv_decode_step")
     return y
@@ -172,7 +183,7 @@ def causal_conv_silu_varlen(x: torch.Tensor, state_pool: torch.Tensor, ids: torc
     assert cu.numel() == ids.numel() + 1, "cu_seqlens must have n_seqs + 1 entries"
     y = torch.empty(N, C, dtype=x.dtype, device=x.device)
     rc = _lib.load().gdn_causal_conv_silu_varlen(
-        _p(x2), xs, _p(state_pool), state_pool.stride(0), state_pool.shape[0], _p(ids), _p(cu),
+        _p(x2), xs, _p(state_pool), _slot_stride(state_pool), state_pool.shape[0], _p(ids), _p(cu),
         ids.numel(), N, C, K, _p(w), _p(y), y.stride(0), _p(status_word(x.device)),
         _stream_ptr(x.device))
     _lib.check(rc, "gdn_causal_conv_silu_varlen")
@@ -223,7 +234,7 @@ def recurrent_gdn_inplace(q, k, v, g, beta, s_pool, ids) -> torch.Tensor:
     assert ids.numel() == bs
     out = torch.empty(bs, 1, HV, DV, dtype=v.dtype, device=v.device)
     rc = _lib.load().gdn_recurrent_inplace(
-        _p(q), qs, _p(k), ks, _p(v), vs, _p(g), _p(beta), _p(s_pool), s_pool.stride(0),
+        _p(q), qs, _p(k), ks, _p(v), vs, _p(g), _p(beta), _p(s_pool), _slot_stride(s_pool),
         s_pool.shape[0], _p(ids), _p(out), bs, HK, HV, DK, DV, DK ** -0.5,
         _p(status_word(v.device)), _stream_ptr(v.device))
     _lib.check(rc, "gdn_recurrent_inplace")
@@ -251,7 +262,7 @@ def chunk_gated_delta_rule_varlen(q, k, v, g, beta, s_pool, ids, cu_seqlens,
     assert cu.numel() == ids.numel() + 1
     out = torch.empty(N, HV, DV, dtype=v.dtype, device=v.device)
     rc = _lib.load().gdn_chunk_prefill_varlen(
-        _p(q), qs, _p(k), ks, _p(v), vs, _p(g), _p(beta), _p(s_pool), s_pool.stride(0),
+        _p(q), qs, _p(k), ks, _p(v), vs, _p(g), _p(beta), _p(s_pool), _slot_stride(s_pool),
         s_pool.shape[0], _p(ids), _p(cu), ids.numel(), N, int(max_seqlen), _p(out), HK, HV, DK,
         DV, DK ** -0.5, _p(status_word(v.device)), _stream_ptr(v.device))
     _lib.check(rc, "gdn_chunk_prefill_varlen")
