@@ -327,21 +327,46 @@ def prefill_bench(pkg, device, steps, peaks):
             m(None, x)
         ctx.reset_context()
 
-    step()
+    for _ in range(2):
+        step()
     torch.cuda.synchronize()
-    t = time_region(step, steps, 1)
-    # chunk kernel alone, on the layer's own conv output
+    per_step = []
+    for _ in range(steps):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        step()
+        e1.record()
+        torch.cuda.synchronize()
+        per_step.append(e0.elapsed_time(e1) / 1e3)
+    t = statistics.median(per_step)
+    # stage breakdown of one step and the chunk kernel alone (CUDA events)
+    stages = {}
     with torch.inference_mode():
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(8)]
+        pools.reset(ids)
+        ev[0].record()
         proj = torch.nn.functional.linear(x, m._fused_weight())
+        ev[1].record()
         r = m._proj_rows
         gg, beta = pkg.ops.fused_g_beta(proj[:, r[1]:r[2]], proj[:, r[2]:r[3]],
                                         m.A_log, m.dt_bias)
+        ev[2].record()
         y = pkg.ops.causal_conv_silu_varlen(proj[:, :m.conv_dim], m.conv_cache, ids,
                                             m.conv1d.weight, cu)
+        ev[3].record()
         q, k, v = m._split(y)
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        pkg.ops.chunk_gated_delta_rule_varlen(q, k, v, gg, beta, m.s_cache, ids, cu, max(lens))
+        o = pkg.ops.chunk_gated_delta_rule_varlen(q, k, v, gg, beta, m.s_cache, ids, cu,
+                                                  max(lens))
+        ev[4].record()
+        core = m.norm(o, proj[:, r[0]:r[1]].view(N, c["HV"], c["DV"]))
+        ev[5].record()
+        m.out_proj(core.view(N, c["HV"] * c["DV"]))
+        ev[6].record()
         torch.cuda.synchronize()
+        for i, name in enumerate(["in_proj_gemm", "gate", "conv", "chunk", "gated_norm",
+                                  "out_proj_gemm"]):
+            stages[name] = round(ev[i].elapsed_time(ev[i + 1]), 3)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record()
         for _ in range(steps):
             pkg.ops.chunk_gated_delta_rule_varlen(q, k, v, gg, beta, m.s_cache, ids, cu,
@@ -354,6 +379,7 @@ def prefill_bench(pkg, device, steps, peaks):
     return {"workload": "config2: 1 GDN layer, 64 seqs, lens U[128,8192] seed 2, "
                         f"{N} tokens, full layer forward",
             "value": round(N / t, 1), "unit": "tok/s", "tokens": N, "ms_per_step": round(t * 1e3, 3),
+            "ms_per_step_min": round(min(per_step) * 1e3, 3), "stages_ms": stages,
             "chunk_kernel": {"kernel": "chunk_prefill", "bound": "tensor",
                              "ms": round(tk * 1e3, 3), "tok_s": round(N / tk, 1),
                              "achieved": round(achieved, 2), "unit": "TFLOP/s",

@@ -198,11 +198,13 @@ class PipelineHandoff:
         assert mode in ("packed", "presum")
         self.H, self.max_tokens, self.dtype, self.device = hidden_size, max_tokens, dtype, device
         self.prev, self.next, self.group, self.mode = peer_prev, peer_next, group, mode
-        parts = 2 if mode == "packed" else 1
-        self._send = [torch.empty(parts, max_tokens, hidden_size, dtype=dtype, device=device)
-                      for _ in range(2)]
-        self._recv = [torch.empty(parts, max_tokens, hidden_size, dtype=dtype, device=device)
-                      for _ in range(2)]
+        self.parts = 2 if mode == "packed" else 1
+        # flat buffers: a message of n tokens is the contiguous prefix viewed
+        # as [parts, n, H], so each part is itself a contiguous [n, H] tensor
+        self._send = [torch.empty(self.parts * max_tokens * hidden_size, dtype=dtype,
+                                  device=device) for _ in range(2)]
+        self._recv = [torch.empty(self.parts * max_tokens * hidden_size, dtype=dtype,
+                                  device=device) for _ in range(2)]
         self._send_work = [None, None]
         self._slot = 0
         self._rslot = 0
@@ -223,7 +225,7 @@ class PipelineHandoff:
         i = self._slot
         self._slot ^= 1
         self._wait_send(i)   # the send that last used this buffer has completed
-        buf = self._send[i][:, :n]
+        buf = self._send[i][:self.parts * n * self.H].view(self.parts, n, self.H)
         if self.mode == "packed":
             buf[0].copy_(hidden)
             buf[1].copy_(residual)
@@ -234,10 +236,9 @@ class PipelineHandoff:
             ev.record(torch.cuda.current_stream(self.device))
             with torch.cuda.stream(self.stream):
                 self.stream.wait_event(ev)
-                self._send_work[i] = dist.isend(buf.contiguous() if not buf.is_contiguous()
-                                                else buf, self.next, group=self.group)
+                self._send_work[i] = dist.isend(buf, self.next, group=self.group)
         else:
-            self._send_work[i] = dist.isend(buf.contiguous(), self.next, group=self.group)
+            self._send_work[i] = dist.isend(buf, self.next, group=self.group)
 
     def recv(self, n: int):
         """Receive the previous stage's message for ``n`` tokens; returns
@@ -247,7 +248,7 @@ class PipelineHandoff:
         assert n <= self.max_tokens
         i = self._rslot
         self._rslot ^= 1
-        buf = self._recv[i][:, :n]
+        buf = self._recv[i][:self.parts * n * self.H].view(self.parts, n, self.H)
         if self.cuda:
             cur = torch.cuda.current_stream(self.device)
             ev0 = torch.cuda.Event()
