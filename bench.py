@@ -237,21 +237,24 @@ def recurrent_kernel_roofline(pkg, stack, peaks, launches):
     gg = -torch.rand(bs, HV, generator=g, device=stack.dev)
     beta = torch.rand(bs, HV, generator=g, device=stack.dev).to(torch.bfloat16)
     views = [m.s_cache for m in stack.layers]
+    # as the layer calls it: gated-RMSNorm epilogue fused (z read, normed output)
+    z = torch.randn(bs, HV, D, generator=g, device=stack.dev).to(torch.bfloat16)
+    nw = torch.ones(D, device=stack.dev, dtype=torch.bfloat16)
     for vw in views[:3]:
-        ops.recurrent_gdn_inplace(q, k, v, gg, beta, vw, stack.ids)
+        ops.recurrent_gdn_inplace(q, k, v, gg, beta, vw, stack.ids, z=z, norm_weight=nw)
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     n = 0
     e0.record()
     for _ in range(launches):
         for vw in views:
-            ops.recurrent_gdn_inplace(q, k, v, gg, beta, vw, stack.ids)
+            ops.recurrent_gdn_inplace(q, k, v, gg, beta, vw, stack.ids, z=z, norm_weight=nw)
             n += 1
     e1.record()
     torch.cuda.synchronize()
     dt = e0.elapsed_time(e1) / 1e3 / n
     state_bytes = 2 * bs * HV * D * D * 4
-    act_bytes = bs * (2 * HK * D + HV * D) * 2 + bs * HV * (4 + 2) + bs * HV * D * 2
+    act_bytes = bs * (2 * HK * D + HV * D) * 2 + bs * HV * (4 + 2) + 2 * bs * HV * D * 2
     algo = state_bytes + act_bytes
     achieved = algo / dt / 1e9
     traffic = read_profile_traffic("recurrent_decode_c1.md")
@@ -355,22 +358,21 @@ def prefill_bench(pkg, device, steps, peaks):
                                             m.conv1d.weight, cu)
         ev[3].record()
         q, k, v = m._split(y)
-        o = pkg.ops.chunk_gated_delta_rule_varlen(q, k, v, gg, beta, m.s_cache, ids, cu,
-                                                  max(lens))
+        z = proj[:, r[0]:r[1]].view(N, c["HV"], c["DV"])
+        core = pkg.ops.chunk_gated_delta_rule_varlen(q, k, v, gg, beta, m.s_cache, ids, cu,
+                                                     max(lens), z=z, norm_weight=m.norm.weight)
         ev[4].record()
-        core = m.norm(o, proj[:, r[0]:r[1]].view(N, c["HV"], c["DV"]))
-        ev[5].record()
         m.out_proj(core.view(N, c["HV"] * c["DV"]))
-        ev[6].record()
+        ev[5].record()
         torch.cuda.synchronize()
-        for i, name in enumerate(["in_proj_gemm", "gate", "conv", "chunk", "gated_norm",
+        for i, name in enumerate(["in_proj_gemm", "gate", "conv", "chunk_with_norm",
                                   "out_proj_gemm"]):
             stages[name] = round(ev[i].elapsed_time(ev[i + 1]), 3)
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record()
         for _ in range(steps):
             pkg.ops.chunk_gated_delta_rule_varlen(q, k, v, gg, beta, m.s_cache, ids, cu,
-                                                  max(lens))
+                                                  max(lens), z=z, norm_weight=m.norm.weight)
         e1.record()
         torch.cuda.synchronize()
     tk = e0.elapsed_time(e1) / 1e3 / steps
@@ -380,7 +382,8 @@ def prefill_bench(pkg, device, steps, peaks):
                         f"{N} tokens, full layer forward",
             "value": round(N / t, 1), "unit": "tok/s", "tokens": N, "ms_per_step": round(t * 1e3, 3),
             "ms_per_step_min": round(min(per_step) * 1e3, 3), "stages_ms": stages,
-            "chunk_kernel": {"kernel": "chunk_prefill", "bound": "tensor",
+            "chunk_kernel": {"kernel": "chunk_prefill_tc_kernel (gated norm fused)",
+                             "bound": "tensor",
                              "ms": round(tk * 1e3, 3), "tok_s": round(N / tk, 1),
                              "achieved": round(achieved, 2), "unit": "TFLOP/s",
                              "peak": peaks["bf16_tflops"], "peak_source": peaks["source"],
@@ -608,7 +611,8 @@ def main():
                        "cuda_graph": True, "parallelism": f"dp{world} (independent sequences)"},
             "state_gbs": round(world * state_bytes_step * args.steps / t / 1e9, 1),
             "e2e": e2e, "roofline": roof,
-            "gpu_launches": 4 * c["layers"] * args.steps,
+            # per layer: gate, conv step, recurrent (+ fused gated norm)
+            "gpu_launches": 3 * c["layers"] * args.steps,
             "clocks": clk}
 
     if rank == 0 and world == 1 and not args.no_prefill:

@@ -38,7 +38,7 @@
 extern "C" {
 #endif
 
-#define GDN_ABI_VERSION 1
+#define GDN_ABI_VERSION 2
 
 enum gdn_status_code {
   GDN_OK = 0,
@@ -132,6 +132,10 @@ int gdn_causal_conv_silu_varlen(const void* x, int64_t x_row_stride,
  * s_pool: fp32 per-layer view [slots, num_v_heads, head_k_dim, head_v_dim]
  * (head, row and column strides dense, as the reference asserts);
  * out: bf16 [bs, num_v_heads, head_v_dim] contiguous.
+ * Optional fused gated-RMSNorm epilogue (Qwen3_5RMSNormGated, qwen3_5.py:121-131,
+ * 697-709): when z != NULL, out receives rms_norm_gated(o, z, norm_weight, norm_eps)
+ * instead of o, with z bf16 rows of num_v_heads*head_v_dim (row stride z_row_stride,
+ * heads contiguous) and norm_weight bf16 [head_v_dim].
  * Supported head dims: (head_k_dim, head_v_dim) in {(64,64), (128,128)}.
  */
 int gdn_recurrent_inplace(const void* q, int64_t q_row_stride,
@@ -142,7 +146,8 @@ int gdn_recurrent_inplace(const void* q, int64_t q_row_stride,
                           const int64_t* ids, void* out,
                           int32_t bs, int32_t num_k_heads, int32_t num_v_heads,
                           int32_t head_k_dim, int32_t head_v_dim, float scale,
-                          int32_t* status, void* stream);
+                          const void* z, int64_t z_row_stride, const void* norm_weight,
+                          float norm_eps, int32_t* status, void* stream);
 
 /*
  * (c) Varlen chunked gated-delta-rule prefill.  Replaces the chunk rule
@@ -154,7 +159,8 @@ int gdn_recurrent_inplace(const void* q, int64_t q_row_stride,
  * rows (out: bf16 [n_tokens, num_v_heads, head_v_dim] contiguous).
  * max_seqlen bounds the longest sequence (context.max_seqlen_q); a longer
  * sequence is truncated to max_seqlen and flagged GDN_STATUS_BAD_SEQLEN.
- * Chunk size 64, as the reference.  Supported head dims as
+ * Chunk size 64, as the reference.  Supported head dims and the optional
+ * gated-RMSNorm epilogue (z, z_row_stride, norm_weight, norm_eps) as
  * gdn_recurrent_inplace.
  */
 int gdn_chunk_prefill_varlen(const void* q, int64_t q_row_stride,
@@ -166,7 +172,8 @@ int gdn_chunk_prefill_varlen(const void* q, int64_t q_row_stride,
                              int32_t n_seqs, int64_t n_tokens, int32_t max_seqlen,
                              void* out, int32_t num_k_heads, int32_t num_v_heads,
                              int32_t head_k_dim, int32_t head_v_dim, float scale,
-                             int32_t* status, void* stream);
+                             const void* z, int64_t z_row_stride, const void* norm_weight,
+                             float norm_eps, int32_t* status, void* stream);
 
 /*
  * Gated RMSNorm over the value head dim.  Replaces Qwen3_5RMSNormGated /

@@ -222,12 +222,13 @@ int chunk_prefill_simt(int n_seqs, int HV, int D, cudaStream_t s, const bf16* q,
 
 bool chunk_tc_supported(int D, const void* q, int64_t qs, const void* k, int64_t ks,
                         const void* v, int64_t vs, const void* out, const void* pool,
-                        int64_t slot_stride);
+                        int64_t slot_stride, const void* z, int64_t zs, const void* nw);
 int chunk_prefill_tc(int n_seqs, int HV, cudaStream_t s, const bf16* q, int64_t qs,
                      const bf16* k, int64_t ks, const bf16* v, int64_t vs, const float* g,
                      const bf16* beta, float* pool, int64_t slot_stride, int64_t num_slots,
                      const int64_t* ids, const int32_t* cu, int64_t n_tokens, int max_seqlen,
-                     bf16* out, int HK, float scale, int32_t* status);
+                     bf16* out, int HK, float scale, const bf16* z, int64_t zs, const bf16* nw,
+                     float eps, int32_t* status);
 
 }  // namespace gdn
 
@@ -241,6 +242,8 @@ extern "C" int gdn_chunk_prefill_varlen(const void* q, int64_t q_row_stride, con
                                         int64_t n_tokens, int32_t max_seqlen, void* out,
                                         int32_t num_k_heads, int32_t num_v_heads,
                                         int32_t head_k_dim, int32_t head_v_dim, float scale,
+                                        const void* z, int64_t z_row_stride,
+                                        const void* norm_weight, float norm_eps,
                                         int32_t* status, void* stream) {
   clear_error();
   GDN_REQUIRE(n_seqs >= 0 && n_tokens >= 0 && max_seqlen >= 0 && num_k_heads > 0 &&
@@ -258,19 +261,26 @@ extern "C" int gdn_chunk_prefill_varlen(const void* q, int64_t q_row_stride, con
               "gdn_chunk_prefill_varlen: row stride smaller than the heads it holds");
   GDN_REQUIRE(num_slots > 0 && slot_stride >= (int64_t)num_v_heads * head_k_dim * head_v_dim,
               "gdn_chunk_prefill_varlen: slot_stride too small");
+  GDN_REQUIRE(z == nullptr || (norm_weight != nullptr &&
+                                z_row_stride >= (int64_t)num_v_heads * head_v_dim),
+              "gdn_chunk_prefill_varlen: fused norm needs norm_weight and z rows of HV*DV");
   if (n_seqs == 0 || n_tokens == 0) return GDN_OK;
   GDN_REQUIRE(q && k && v && g && beta && s_pool && ids && cu_seqlens && out,
               "gdn_chunk_prefill_varlen: null pointer");
+  cudaStream_t s = (cudaStream_t)stream;
   if (chunk_tc_supported(head_k_dim, q, q_row_stride, k, k_row_stride, v, v_row_stride, out,
-                         s_pool, slot_stride))
-    return chunk_prefill_tc(n_seqs, num_v_heads, (cudaStream_t)stream, (const bf16*)q,
-                            q_row_stride, (const bf16*)k, k_row_stride, (const bf16*)v,
-                            v_row_stride, g, (const bf16*)beta, s_pool, slot_stride, num_slots,
-                            ids, cu_seqlens, n_tokens, max_seqlen, (bf16*)out, num_k_heads, scale,
-                            status);
-  return chunk_prefill_simt(n_seqs, num_v_heads, head_k_dim, (cudaStream_t)stream, (const bf16*)q,
-                            q_row_stride, (const bf16*)k, k_row_stride, (const bf16*)v,
-                            v_row_stride, g, (const bf16*)beta, s_pool, slot_stride, num_slots,
-                            ids, cu_seqlens, n_tokens, max_seqlen, (bf16*)out, num_k_heads, scale,
-                            status);
+                         s_pool, slot_stride, z, z_row_stride, norm_weight))
+    return chunk_prefill_tc(n_seqs, num_v_heads, s, (const bf16*)q, q_row_stride, (const bf16*)k,
+                            k_row_stride, (const bf16*)v, v_row_stride, g, (const bf16*)beta,
+                            s_pool, slot_stride, num_slots, ids, cu_seqlens, n_tokens, max_seqlen,
+                            (bf16*)out, num_k_heads, scale, (const bf16*)z, z_row_stride,
+                            (const bf16*)norm_weight, norm_eps, status);
+  int rc = chunk_prefill_simt(n_seqs, num_v_heads, head_k_dim, s, (const bf16*)q, q_row_stride,
+                              (const bf16*)k, k_row_stride, (const bf16*)v, v_row_stride, g,
+                              (const bf16*)beta, s_pool, slot_stride, num_slots, ids, cu_seqlens,
+                              n_tokens, max_seqlen, (bf16*)out, num_k_heads, scale, status);
+  if (rc == GDN_OK && z != nullptr)   // the fp32 kernel stores o; norm it in place
+    rc = launch_rms_norm_gated(out, z, z_row_stride, num_v_heads, norm_weight, out,
+                               n_tokens * num_v_heads, head_v_dim, norm_eps, s);
+  return rc;
 }

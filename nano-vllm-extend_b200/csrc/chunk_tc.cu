@@ -620,7 +620,7 @@ __global__ void __launch_bounds__(kThreads, 2) chunk_prefill_tc_kernel(
 
 bool chunk_tc_supported(int D, const void* q, int64_t qs, const void* k, int64_t ks,
                         const void* v, int64_t vs, const void* out, const void* pool,
-                        int64_t slot_stride) {
+                        int64_t slot_stride, const void*, int64_t, const void*) {
   return D == tc::kD && aligned16(q) && aligned16(k) && aligned16(v) && aligned16(out) &&
          aligned16(pool) && qs % 8 == 0 && ks % 8 == 0 && vs % 8 == 0 && slot_stride % 4 == 0;
 }
@@ -662,7 +662,8 @@ int chunk_prefill_tc(int n_seqs, int HV, cudaStream_t s, const bf16* q, int64_t 
                      const bf16* k, int64_t ks, const bf16* v, int64_t vs, const float* g,
                      const bf16* beta, float* pool, int64_t slot_stride, int64_t num_slots,
                      const int64_t* ids, const int32_t* cu, int64_t n_tokens, int max_seqlen,
-                     bf16* out, int HK, float scale, int32_t* status) {
+                     bf16* out, int HK, float scale, const bf16* z, int64_t zs, const bf16* nw,
+                     float eps, int32_t* status) {
   CUtensorMap tm_q, tm_k, tm_v;
   if (!make_tile_map(&tm_q, q, (int64_t)HK * tc::kD, n_tokens, qs) ||
       !make_tile_map(&tm_k, k, (int64_t)HK * tc::kD, n_tokens, ks) ||
@@ -680,7 +681,12 @@ int chunk_prefill_tc(int n_seqs, int HV, cudaStream_t s, const bf16* q, int64_t 
   tc::chunk_prefill_tc_kernel<<<(unsigned)((int64_t)n_seqs * HV), tc::kThreads, smem, s>>>(
       tm_q, tm_k, tm_v, g, beta, pool, slot_stride, num_slots, ids, cu, n_tokens, max_seqlen,
       out, HK, HV, scale, status);
-  return check_launch("gdn_chunk_prefill_varlen");
+  int rc = check_launch("gdn_chunk_prefill_varlen");
+  // gated RMSNorm in place over the output rows (a full-occupancy kernel; an
+  // epilogue inside this kernel would run on half its threads)
+  if (rc == GDN_OK && z != nullptr)
+    rc = launch_rms_norm_gated(out, z, zs, HV, nw, out, n_tokens * HV, tc::kD, eps, s);
+  return rc;
 }
 
 }  // namespace gdn

@@ -21,6 +21,15 @@ int check_launch(const char* what);
 // Number of SMs of the current device (cached per device).
 int sm_count();
 
+// Gated RMSNorm launch (gate_norm.cu); x and y may alias (in place).
+int launch_rms_norm_gated(const void* x, const void* gate, int64_t gate_token_stride,
+                          int heads_per_token, const void* weight, void* y, int64_t n_rows,
+                          int dim, float eps, cudaStream_t s);
+
+// The reference's gated-norm rounding for one element (qwen3_5.py:127-131):
+// y = bf16(bf16(w * bf16(x * inv)) * silu(z)), fp32 arithmetic.
+__device__ __forceinline__ float gated_norm_elem(float x, float inv, float w, float z);
+
 #define GDN_REQUIRE(cond, ...)                       \
   do {                                               \
     if (!(cond)) {                                   \
@@ -45,6 +54,12 @@ __device__ __forceinline__ float round_bf(float x) { return __bfloat162float(__f
 
 __device__ __forceinline__ float sigmoidf_(float x) { return 1.0f / (1.0f + expf(-x)); }
 __device__ __forceinline__ float siluf_(float x) { return x * sigmoidf_(x); }
+
+__device__ __forceinline__ float gated_norm_elem(float x, float inv, float w, float z) {
+  const float t = __bfloat162float(__float2bfloat16_rn(x * inv));
+  const float u = __bfloat162float(__float2bfloat16_rn(w * t));
+  return u * siluf_(z);
+}
 
 // 8 packed bf16 <-> 8 floats
 __device__ __forceinline__ void unpack8(const uint4& u, float* f) {

@@ -38,37 +38,76 @@ __global__ void __launch_bounds__(256) gbeta_kernel(
   }
 }
 
-// One warp per row: y = bf16(bf16(w * bf16(x * rsqrt(mean x^2 + eps))) * silu(gate)),
-// the rounding sequence of qwen3_5.py:121-131 for a bf16 model.
+// Gated RMSNorm, y = bf16(bf16(w * bf16(x * rsqrt(mean x^2 + eps))) * silu(gate)), the
+// rounding sequence of qwen3_5.py:121-131 for a bf16 model.  Each lane moves 8
+// elements as 16-byte vectors; DIM/8 lanes share a row and reduce by shuffles.
+// x and y may alias: a row's lanes read it fully before any of them writes.
 template <int DIM>
 __global__ void __launch_bounds__(256) rms_gated_kernel(
-    const bf16* __restrict__ x, const bf16* __restrict__ gate, int64_t gate_token_stride,
-    int heads, const bf16* __restrict__ w, bf16* __restrict__ y, int64_t n_rows, float eps) {
-  constexpr int PER = DIM / 32;
+    const bf16* x, const bf16* __restrict__ gate, int64_t gate_token_stride,
+    int heads, const bf16* __restrict__ w, bf16* y, int64_t n_rows, float eps) {
+  constexpr int LPR = DIM / 8;                 // lanes per row
+  constexpr int RPW = 32 / LPR;                // rows per warp
   const int lane = threadIdx.x & 31;
-  const int64_t warps_total = (int64_t)gridDim.x * (blockDim.x >> 5);
-  for (int64_t row = blockIdx.x * (int64_t)(blockDim.x >> 5) + (threadIdx.x >> 5); row < n_rows;
-       row += warps_total) {
-    float xv[PER];
+  const int sub = lane % LPR;
+  float wv[8];
+  unpack8(*reinterpret_cast<const uint4*>(w + sub * 8), wv);
+  const int64_t rows_per_iter = (int64_t)gridDim.x * (blockDim.x >> 5) * RPW;
+  // warp-uniform loop bound: every lane of a warp runs the same iterations
+  for (int64_t base = ((int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5)) * RPW;
+       base < n_rows; base += rows_per_iter) {
+    const int64_t row = base + lane / LPR;
+    const bool active = row < n_rows;
+    float xv[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f}, gv[8];
+    if (active) {
+      unpack8(*reinterpret_cast<const uint4*>(x + row * DIM + sub * 8), xv);
+      const int64_t tok = row / heads;
+      unpack8(*reinterpret_cast<const uint4*>(gate + tok * gate_token_stride +
+                                              (row - tok * heads) * DIM + sub * 8),
+              gv);
+    }
     float ss = 0.f;
 #pragma unroll
-    for (int i = 0; i < PER; ++i) {
-      xv[i] = bf2f(x[row * DIM + lane + 32 * i]);
-      ss += xv[i] * xv[i];
-    }
-    ss = warp_sum(ss);
-    const float inv = rsqrtf(ss / (float)DIM + eps);
-    const int64_t tok = row / heads;
-    const bf16* grow = gate + tok * gate_token_stride + (row - tok * heads) * DIM;
+    for (int e = 0; e < 8; ++e) ss += xv[e] * xv[e];
 #pragma unroll
-    for (int i = 0; i < PER; ++i) {
-      const int c = lane + 32 * i;
-      const float t = round_bf(xv[i] * inv);
-      const float u = round_bf(bf2f(w[c]) * t);
-      const float gz = bf2f(grow[c]);
-      y[row * DIM + c] = f2bf(u * siluf_(gz));
+    for (int o = LPR / 2; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    const float inv = rsqrtf(ss / (float)DIM + eps);
+    if (active) {
+      float yv[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) yv[e] = gated_norm_elem(xv[e], inv, wv[e], gv[e]);
+      *reinterpret_cast<uint4*>(y + row * DIM + sub * 8) = pack8(yv);
     }
   }
+}
+
+int launch_rms_norm_gated(const void* x, const void* gate, int64_t gate_token_stride,
+                          int heads_per_token, const void* weight, void* y, int64_t n_rows,
+                          int dim, float eps, cudaStream_t s) {
+  if (n_rows == 0) return GDN_OK;
+  GDN_UNSUPPORTED(((uintptr_t)x | (uintptr_t)gate | (uintptr_t)weight | (uintptr_t)y) % 16 == 0 &&
+                      gate_token_stride % 8 == 0,
+                  "gated norm: operands must be 16-byte aligned");
+  int64_t blocks = (n_rows + 31) / 32;
+  const int64_t cap = (int64_t)sm_count() * 8;
+  if (blocks > cap) blocks = cap;
+#define GDN_NORM_CASE(D)                                                                        \
+  case D:                                                                                       \
+    rms_gated_kernel<D><<<(unsigned)blocks, 256, 0, s>>>((const bf16*)x, (const bf16*)gate,    \
+                                                         gate_token_stride, heads_per_token,    \
+                                                         (const bf16*)weight, (bf16*)y, n_rows, \
+                                                         eps);                                  \
+    break;
+  switch (dim) {
+    GDN_NORM_CASE(64)
+    GDN_NORM_CASE(128)
+    GDN_NORM_CASE(256)
+    default:
+      set_error("gated norm: dim %d unsupported", dim);
+      return GDN_ERR_UNSUPPORTED;
+  }
+#undef GDN_NORM_CASE
+  return check_launch("gated norm");
 }
 
 }  // namespace gdn
@@ -118,22 +157,6 @@ extern "C" int gdn_rms_norm_gated(const void* x, const void* gate, int64_t gate_
               "gdn_rms_norm_gated: gate token stride < heads_per_token * dim");
   if (n_rows == 0) return GDN_OK;
   GDN_REQUIRE(x && gate && weight && y, "gdn_rms_norm_gated: null pointer");
-  int64_t blocks = (n_rows + 7) / 8;
-  const int64_t cap = (int64_t)sm_count() * 16;
-  if (blocks > cap) blocks = cap;
-  cudaStream_t s = (cudaStream_t)stream;
-#define GDN_NORM_CASE(D)                                                                      \
-  case D:                                                                                     \
-    rms_gated_kernel<D><<<(unsigned)blocks, 256, 0, s>>>((const bf16*)x, (const bf16*)gate,  \
-                                                         gate_token_stride, heads_per_token,  \
-                                                         (const bf16*)weight,                 \
-                                                         (bf16*)y, n_rows, eps);              \
-    break;
-  switch (dim) {
-    GDN_NORM_CASE(64)
-    GDN_NORM_CASE(128)
-    GDN_NORM_CASE(256)
-  }
-#undef GDN_NORM_CASE
-  return check_launch("gdn_rms_norm_gated");
+  return launch_rms_norm_gated(x, gate, gate_token_stride, heads_per_token, weight, y, n_rows,
+                               dim, eps, (cudaStream_t)stream);
 }

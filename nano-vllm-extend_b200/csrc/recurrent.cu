@@ -20,13 +20,17 @@
 
 namespace gdn {
 
-template <int DK, int DV, int DVT, int NT>
+// NORM: the output row (all DV columns live in this CTA, DVT == DV) goes
+// through the gated RMSNorm before it is stored (qwen3_5.py:121-131).
+template <int DK, int DV, int DVT, int NT, bool NORM>
 __global__ void __launch_bounds__(NT) recurrent_inplace_kernel(
     const bf16* __restrict__ q, int64_t qs, const bf16* __restrict__ k, int64_t ks,
     const bf16* __restrict__ v, int64_t vs, const float* __restrict__ g,
     const bf16* __restrict__ beta, float* __restrict__ pool, int64_t slot_stride,
     int64_t num_slots, const int64_t* __restrict__ ids, bf16* __restrict__ out, int HK, int HV,
-    float scale, int32_t* status) {
+    float scale, const bf16* __restrict__ z, int64_t zs, const bf16* __restrict__ nw, float eps,
+    int32_t* status) {
+  static_assert(!NORM || DVT == DV, "the fused norm needs the whole row in one CTA");
   constexpr int VS = DV / DVT;   // column slices per unit
   constexpr int CG = DVT / 4;    // threads across a row (float4 each)
   constexpr int RG = NT / CG;    // rows per pass
@@ -39,6 +43,7 @@ __global__ void __launch_bounds__(NT) recurrent_inplace_kernel(
   __shared__ __align__(16) float sdelta[DVT];
   __shared__ float sq[DK], sk[DK], sv[DVT];
   __shared__ float snorm[2];
+  __shared__ float swsum[NT / 32];
 
   const int unit = blockIdx.x / VS;
   const int vt = blockIdx.x - unit * VS;
@@ -58,6 +63,15 @@ __global__ void __launch_bounds__(NT) recurrent_inplace_kernel(
 #pragma unroll
   for (int i = 0; i < RPT; ++i)
     s[i] = __ldcs(reinterpret_cast<const float4*>(sbase + (int64_t)(r0 + RG * i) * DV));
+
+  // the norm epilogue's z and weight are fetched now, not at the tail
+  float zval = 0.f, wval = 0.f;
+  if constexpr (NORM) {
+    if (tid < DVT) {
+      zval = bf2f(z[(int64_t)b * zs + h * DV + tid]);
+      wval = bf2f(nw[tid]);
+    }
+  }
 
   // q, k, v of this unit (fp32 in shared memory); norms by warp 0.
   for (int i = tid; i < DK; i += NT) {
@@ -117,11 +131,24 @@ __global__ void __launch_bounds__(NT) recurrent_inplace_kernel(
   }
   *reinterpret_cast<float4*>(&red[r0][4 * c4]) = acc;
   __syncthreads();
+  float o = 0.f;
   if (tid < DVT) {
-    float o = 0.f;
 #pragma unroll
     for (int j = 0; j < RG; ++j) o += red[j][tid];
-    out[((int64_t)b * HV + h) * DV + vt * DVT + tid] = f2bf(o);
+  }
+  bf16* orow = out + ((int64_t)b * HV + h) * DV + vt * DVT;
+  if constexpr (!NORM) {
+    if (tid < DVT) orow[tid] = f2bf(o);
+  } else {
+    const float x = tid < DVT ? round_bf(o) : 0.f;   // the core output is bf16 first
+    const float ss = warp_sum(x * x);
+    if ((tid & 31) == 0) swsum[tid >> 5] = ss;
+    __syncthreads();
+    float tot = 0.f;
+#pragma unroll
+    for (int w = 0; w < NT / 32; ++w) tot += swsum[w];
+    const float inv = rsqrtf(tot / (float)DV + eps);
+    if (tid < DVT) orow[tid] = f2bf(gated_norm_elem(x, inv, wval, zval));
   }
 }
 
@@ -130,9 +157,16 @@ static void launch_recurrent(dim3 grid, cudaStream_t s, const bf16* q, int64_t q
                              int64_t ks, const bf16* v, int64_t vs, const float* g,
                              const bf16* beta, float* pool, int64_t slot_stride, int64_t num_slots,
                              const int64_t* ids, bf16* out, int HK, int HV, float scale,
+                             const bf16* z, int64_t zs, const bf16* nw, float eps,
                              int32_t* status) {
-  recurrent_inplace_kernel<DK, DV, DVT, NT><<<grid, NT, 0, s>>>(
-      q, qs, k, ks, v, vs, g, beta, pool, slot_stride, num_slots, ids, out, HK, HV, scale, status);
+  if (z != nullptr && DVT == DV)
+    recurrent_inplace_kernel<DK, DV, DVT, NT, (DVT == DV)><<<grid, NT, 0, s>>>(
+        q, qs, k, ks, v, vs, g, beta, pool, slot_stride, num_slots, ids, out, HK, HV, scale, z,
+        zs, nw, eps, status);
+  else
+    recurrent_inplace_kernel<DK, DV, DVT, NT, false><<<grid, NT, 0, s>>>(
+        q, qs, k, ks, v, vs, g, beta, pool, slot_stride, num_slots, ids, out, HK, HV, scale, z,
+        zs, nw, eps, status);
 }
 
 }  // namespace gdn
@@ -145,7 +179,9 @@ extern "C" int gdn_recurrent_inplace(const void* q, int64_t q_row_stride, const 
                                      int64_t slot_stride, int64_t num_slots, const int64_t* ids,
                                      void* out, int32_t bs, int32_t num_k_heads,
                                      int32_t num_v_heads, int32_t head_k_dim, int32_t head_v_dim,
-                                     float scale, int32_t* status, void* stream) {
+                                     float scale, const void* z, int64_t z_row_stride,
+                                     const void* norm_weight, float norm_eps, int32_t* status,
+                                     void* stream) {
   clear_error();
   GDN_REQUIRE(bs >= 0 && num_k_heads > 0 && num_v_heads > 0,
               "gdn_recurrent_inplace: bad sizes (bs=%d, HK=%d, HV=%d)", bs, num_k_heads,
@@ -163,6 +199,9 @@ extern "C" int gdn_recurrent_inplace(const void* q, int64_t q_row_stride, const 
                   slot_stride % 4 == 0,
               "gdn_recurrent_inplace: slot_stride %lld must be >= HV*DK*DV and a multiple of 4",
               (long long)slot_stride);
+  GDN_REQUIRE(z == nullptr || (norm_weight != nullptr &&
+                                z_row_stride >= (int64_t)num_v_heads * head_v_dim),
+              "gdn_recurrent_inplace: fused norm needs norm_weight and z rows of HV*DV");
   if (bs == 0) return GDN_OK;
   GDN_REQUIRE(q && k && v && g && beta && s_pool && ids && out, "gdn_recurrent_inplace: null pointer");
   GDN_REQUIRE(aligned16(s_pool), "gdn_recurrent_inplace: s_pool must be 16-byte aligned");
@@ -178,24 +217,32 @@ extern "C" int gdn_recurrent_inplace(const void* q, int64_t q_row_stride, const 
       launch_recurrent<128, 128, 128, 256>(dim3((unsigned)units), s, qb, q_row_stride, kb,
                                            k_row_stride, vb, v_row_stride, g, bb, s_pool,
                                            slot_stride, num_slots, ids, ob, num_k_heads,
-                                           num_v_heads, scale, status);
+                                           num_v_heads, scale, (const bf16*)z, z_row_stride,
+                                           (const bf16*)norm_weight, norm_eps, status);
     } else {
       launch_recurrent<128, 128, 32, 128>(dim3((unsigned)(units * 4)), s, qb, q_row_stride, kb,
                                           k_row_stride, vb, v_row_stride, g, bb, s_pool,
                                           slot_stride, num_slots, ids, ob, num_k_heads,
-                                          num_v_heads, scale, status);
+                                          num_v_heads, scale, (const bf16*)z, z_row_stride,
+                                           (const bf16*)norm_weight, norm_eps, status);
     }
   } else {
     if (units >= target) {
       launch_recurrent<64, 64, 64, 128>(dim3((unsigned)units), s, qb, q_row_stride, kb,
                                         k_row_stride, vb, v_row_stride, g, bb, s_pool, slot_stride,
                                         num_slots, ids, ob, num_k_heads, num_v_heads, scale,
-                                        status);
+                                        (const bf16*)z, z_row_stride, (const bf16*)norm_weight,
+                                        norm_eps, status);
     } else {
       launch_recurrent<64, 64, 16, 64>(dim3((unsigned)(units * 4)), s, qb, q_row_stride, kb,
                                        k_row_stride, vb, v_row_stride, g, bb, s_pool, slot_stride,
-                                       num_slots, ids, ob, num_k_heads, num_v_heads, scale, status);
+                                       num_slots, ids, ob, num_k_heads, num_v_heads, scale, (const bf16*)z, z_row_stride,
+                                           (const bf16*)norm_weight, norm_eps, status);
     }
   }
-  return check_launch("gdn_recurrent_inplace");
+  int rc = check_launch("gdn_recurrent_inplace");
+  if (rc == GDN_OK && z != nullptr && units < target)   // column-split launch: norm after
+    rc = launch_rms_norm_gated(out, z, z_row_stride, num_v_heads, norm_weight, out, units,
+                               head_v_dim, norm_eps, s);
+  return rc;
 }

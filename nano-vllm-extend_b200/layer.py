@@ -169,16 +169,16 @@ class Qwen3_5GatedDeltaNet(nn.Module):
             n1 = 0
             while n1 < len(lens_q) and lens_q[n1] == 1:
                 n1 += 1
+        # the gated RMSNorm (self.norm) runs fused in each core kernel's epilogue
         outs = []
         if n1:
-            outs.append(self._decode_core(mixed[:n1], g[:n1], beta[:n1], ids[:n1]))
+            outs.append(self._decode_core(mixed[:n1], g[:n1], beta[:n1], ids[:n1], z[:n1]))
         if n1 < N:
             cu_q = ctx.cu_seqlens_q
             cu_p = cu_q[n1:] - cu_q[n1] if n1 else cu_q
             outs.append(self._prefill_core(mixed[n1:], g[n1:], beta[n1:], ids[n1:], cu_p,
-                                           max(lens_q[n1:])))
-        core = outs[0] if len(outs) == 1 else torch.cat(outs, 0)    # [N, HV, DV]
-        core = self.norm(core, z)
+                                           max(lens_q[n1:]), z[n1:]))
+        core = outs[0] if len(outs) == 1 else torch.cat(outs, 0)    # [N, HV, DV], normed
         return self.out_proj(core.view(N, vd))
 
     def _split(self, y: torch.Tensor):
@@ -189,23 +189,26 @@ class Qwen3_5GatedDeltaNet(nn.Module):
         v = y[:, 2 * kd:].view(n, self.num_v_heads, self.head_v_dim)
         return q, k, v
 
-    def _decode_core(self, mixed, g, beta, ids):
-        """T == 1 rows: conv step + in-place recurrent (qwen3_5.py:1008-1026)."""
+    def _decode_core(self, mixed, g, beta, ids, z):
+        """T == 1 rows: conv step + in-place recurrent + gated norm
+        (qwen3_5.py:1008-1026, 1083-1085)."""
         y = ops.conv_decode_step(mixed, self.conv_cache, ids,
                                  self.conv1d.weight.view(self.conv_dim, self.conv_kernel))
         q, k, v = self._split(y)
-        o = ops.recurrent_gdn_inplace(q, k, v, g, beta, self.s_cache, ids)
+        o = ops.recurrent_gdn_inplace(q, k, v, g, beta, self.s_cache, ids, z=z,
+                                      norm_weight=self.norm.weight, eps=self.norm.eps)
         return o.view(-1, self.num_v_heads, self.head_v_dim)
 
-    def _prefill_core(self, mixed, g, beta, ids, cu_seqlens, max_seqlen):
-        """Prefill rows: varlen conv + chunked rule with slot states
-        (the composition of qwen3_5.py:922-963, unpadded)."""
+    def _prefill_core(self, mixed, g, beta, ids, cu_seqlens, max_seqlen, z):
+        """Prefill rows: varlen conv + chunked rule with slot states + gated
+        norm (the composition of qwen3_5.py:922-963, unpadded)."""
         y = ops.causal_conv_silu_varlen(mixed, self.conv_cache, ids,
                                         self.conv1d.weight.view(self.conv_dim, self.conv_kernel),
                                         cu_seqlens)
         q, k, v = self._split(y)
         return ops.chunk_gated_delta_rule_varlen(q, k, v, g, beta, self.s_cache, ids, cu_seqlens,
-                                                 max_seqlen)
+                                                 max_seqlen, z=z, norm_weight=self.norm.weight,
+                                                 eps=self.norm.eps)
 
 
 def install(qwen3_5_module=None, parallel_module=None, context_module=None):

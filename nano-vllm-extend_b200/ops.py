@@ -214,11 +214,29 @@ def _state_view_check(s_pool: torch.Tensor, HV: int, DK: int, DV: int):
     assert s_pool.stride(1) == DK * DV and s_pool.stride(2) == DV and s_pool.stride(3) == 1
 
 
-def recurrent_gdn_inplace(q, k, v, g, beta, s_pool, ids) -> torch.Tensor:
+def _norm_args(z, norm_weight, rows, HV, DV):
+    """(z pointer, z row stride, weight pointer) of the optional fused
+    gated-RMSNorm epilogue; z is [rows, HV, DV] (token stride may exceed
+    HV*DV, heads dense) or None."""
+    if z is None:
+        return None, 0, None
+    assert norm_weight is not None and norm_weight.dtype == torch.bfloat16
+    assert norm_weight.numel() == DV
+    z3 = z.reshape(rows, HV, DV) if z.is_contiguous() else z
+    assert z3.dim() == 3 and tuple(z3.shape) == (rows, HV, DV) and z3.dtype == torch.bfloat16
+    assert z3.stride(2) == 1 and (HV == 1 or z3.stride(1) == DV), "z heads must be dense"
+    return z3, z3.stride(0), norm_weight.contiguous()
+
+
+def recurrent_gdn_inplace(q, k, v, g, beta, s_pool, ids, z=None, norm_weight=None,
+                          eps: float = 1e-6) -> torch.Tensor:
     """qwen3_5.py:596-613.  q/k [bs, 1, HK, DK] (or HK == HV, already
     repeated), v [bs, 1, HV, DV] — strided row views allowed; g fp32 /
     beta bf16 [bs, 1, HV]; s_pool [slots, HV, DK, DV] fp32 per-layer view,
-    rows ``ids`` updated in place.  Returns out [bs, 1, HV, DV] bf16."""
+    rows ``ids`` updated in place.  Returns out [bs, 1, HV, DV] bf16.
+    With ``z`` ([bs, HV, DV]) and ``norm_weight`` the output is the gated
+    RMSNorm of the core output (Qwen3_5RMSNormGated, qwen3_5.py:697-709),
+    fused into the kernel's epilogue."""
     _cuda(q, k, v, g, beta, s_pool, ids)
     bs, HK, DK, qs = _heads(q, "q")
     bs_k, HK_k, DK_k, ks = _heads(k, "k")
@@ -232,21 +250,25 @@ def recurrent_gdn_inplace(q, k, v, g, beta, s_pool, ids) -> torch.Tensor:
     _state_view_check(s_pool, HV, DK, DV)
     ids = _ids64(ids)
     assert ids.numel() == bs
+    z3, zs, nw = _norm_args(z, norm_weight, bs, HV, DV)
     out = torch.empty(bs, 1, HV, DV, dtype=v.dtype, device=v.device)
     rc = _lib.load().gdn_recurrent_inplace(
         _p(q), qs, _p(k), ks, _p(v), vs, _p(g), _p(beta), _p(s_pool), _slot_stride(s_pool),
-        s_pool.shape[0], _p(ids), _p(out), bs, HK, HV, DK, DV, DK ** -0.5,
-        _p(status_word(v.device)), _stream_ptr(v.device))
+        s_pool.shape[0], _p(ids), _p(out), bs, HK, HV, DK, DV, DK ** -0.5, _p(z3), zs, _p(nw),
+        float(eps), _p(status_word(v.device)), _stream_ptr(v.device))
     _lib.check(rc, "gdn_recurrent_inplace")
     return out
 
 
 def chunk_gated_delta_rule_varlen(q, k, v, g, beta, s_pool, ids, cu_seqlens,
-                                  max_seqlen: int) -> torch.Tensor:
+                                  max_seqlen: int, z=None, norm_weight=None,
+                                  eps: float = 1e-6) -> torch.Tensor:
     """Varlen chunked prefill (the chunk rule of qwen3_5.py:140-227 driven by
     cu_seqlens as at :956-961), initial state read from and final state
     written to ``s_pool[ids[r]]``.  q/k [N, HK, DK], v [N, HV, DV] (row
-    views allowed), g fp32 / beta bf16 [N, HV].  Returns out [N, HV, DV]."""
+    views allowed), g fp32 / beta bf16 [N, HV].  Returns out [N, HV, DV];
+    with ``z`` / ``norm_weight`` the gated RMSNorm is fused as in
+    :func:`recurrent_gdn_inplace`."""
     _cuda(q, k, v, g, beta, s_pool, ids, cu_seqlens)
     N, HK, DK, qs = _heads(q, "q")
     N_k, HK_k, DK_k, ks = _heads(k, "k")
@@ -260,11 +282,13 @@ def chunk_gated_delta_rule_varlen(q, k, v, g, beta, s_pool, ids, cu_seqlens,
     cu = cu_seqlens.to(torch.int32).contiguous() if cu_seqlens.dtype != torch.int32 \
         else cu_seqlens.contiguous()
     assert cu.numel() == ids.numel() + 1
+    z3, zs, nw = _norm_args(z, norm_weight, N, HV, DV)
     out = torch.empty(N, HV, DV, dtype=v.dtype, device=v.device)
     rc = _lib.load().gdn_chunk_prefill_varlen(
         _p(q), qs, _p(k), ks, _p(v), vs, _p(g), _p(beta), _p(s_pool), _slot_stride(s_pool),
         s_pool.shape[0], _p(ids), _p(cu), ids.numel(), N, int(max_seqlen), _p(out), HK, HV, DK,
-        DV, DK ** -0.5, _p(status_word(v.device)), _stream_ptr(v.device))
+        DV, DK ** -0.5, _p(z3), zs, _p(nw), float(eps), _p(status_word(v.device)),
+        _stream_ptr(v.device))
     _lib.check(rc, "gdn_chunk_prefill_varlen")
     return out
 

@@ -48,15 +48,17 @@ def test_host_validation_errors(pkg):
     L = pkg._lib
     # recurrent: unsupported head dims -> GDN_ERR_UNSUPPORTED
     rc, msg = _call(pkg, "gdn_recurrent_inplace", None, 96, None, 96, None, 96, None, None, None,
-                    0, 1, None, None, 1, 1, 1, 96, 96, 0.1, None, None)
+                    0, 1, None, None, 1, 1, 1, 96, 96, 0.1, None, 0, None, 1e-6, None, None)
     assert rc == L.GDN_ERR_UNSUPPORTED and "head dims" in msg
     # recurrent: HV not a multiple of HK -> invalid argument
     rc, msg = _call(pkg, "gdn_recurrent_inplace", None, 1024, None, 1024, None, 1024, None, None,
-                    None, 1 << 20, 1, None, None, 1, 3, 4, 128, 128, 0.1, None, None)
+                    None, 1 << 20, 1, None, None, 1, 3, 4, 128, 128, 0.1, None, 0, None, 1e-6,
+                    None, None)
     assert rc == L.GDN_ERR_INVALID_ARGUMENT and "multiple" in msg
     # recurrent: slot stride smaller than one slot
     rc, msg = _call(pkg, "gdn_recurrent_inplace", None, 512, None, 512, None, 512, None, None,
-                    None, 100, 1, None, None, 1, 4, 4, 128, 128, 0.1, None, None)
+                    None, 100, 1, None, None, 1, 4, 4, 128, 128, 0.1, None, 0, None, 1e-6,
+                    None, None)
     assert rc == L.GDN_ERR_INVALID_ARGUMENT and "slot_stride" in msg
     # conv: unsupported kernel width
     rc, msg = _call(pkg, "gdn_conv_decode_step", None, 64, None, 1000, 2, None, 1, 64, 5, None,
@@ -75,14 +77,21 @@ def test_host_validation_errors(pkg):
     assert rc == L.GDN_ERR_UNSUPPORTED
     # chunk: unsupported dims
     rc, msg = _call(pkg, "gdn_chunk_prefill_varlen", None, 64, None, 64, None, 64, None, None,
-                    None, 1 << 20, 2, None, None, 1, 1, 1, None, 1, 1, 32, 32, 0.1, None, None)
+                    None, 1 << 20, 2, None, None, 1, 1, 1, None, 1, 1, 32, 32, 0.1, None, 0, None,
+                    1e-6, None, None)
     assert rc == L.GDN_ERR_UNSUPPORTED
 
 
 def test_empty_calls_are_noops(pkg):
     L = pkg._lib
     assert _call(pkg, "gdn_recurrent_inplace", None, 512, None, 512, None, 1024, None, None, None,
-                 1 << 20, 2, None, None, 0, 4, 8, 128, 128, 0.1, None, None)[0] == L.GDN_OK
+                 1 << 20, 2, None, None, 0, 4, 8, 128, 128, 0.1, None, 0, None, 1e-6, None,
+                 None)[0] == L.GDN_OK
+    # fused norm without a weight is rejected on the host
+    rc, msg = _call(pkg, "gdn_recurrent_inplace", None, 512, None, 512, None, 1024, None, None,
+                    None, 1 << 20, 2, None, None, 0, 4, 8, 128, 128, 0.1, 1, 1024, None, 1e-6,
+                    None, None)
+    assert rc == L.GDN_ERR_INVALID_ARGUMENT and "norm" in msg
     assert _call(pkg, "gdn_fused_g_beta", None, None, 8, 0, 8, None, None, 0, None, None, None,
                  None)[0] == L.GDN_OK
 

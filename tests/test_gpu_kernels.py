@@ -334,3 +334,51 @@ def test_rms_gated_golden(ops, golden_dir):
     zz = bf(np.concatenate([d["z"].reshape(6, 512), np.zeros((6, 40), np.float32)], 1))
     y2 = ops.rms_norm_gated(bf(d["x"]), zz[:, :512].view(6, 8, 64), bf(d["w"]), 1e-6)
     assert torch.equal(y, y2)
+
+
+# ---------------------------------------------------------------------------
+# fused gated-RMSNorm epilogues
+# ---------------------------------------------------------------------------
+
+
+@pytest.mark.parametrize("bs", [64, 2])   # full-tile (fused) and column-split (norm after)
+def test_recurrent_fused_norm(ops, bs):
+    HK, HV, D = 16, 32, 128
+    q, k, v, g, beta = I.core_inputs(bs, HK, D, HV, D, seed=61)
+    q, k, v, beta = (O.round_bf16(t) for t in (q, k, v, beta))
+    r = I.rng(62)
+    pool = (r.standard_normal((bs + 1, HV, D, D)) * 0.02).astype(np.float32)
+    zbig = O.round_bf16(r.standard_normal((bs, HV * D + 24)).astype(np.float32))
+    w = O.round_bf16((1 + 0.1 * r.standard_normal(D)).astype(np.float32))
+    ids = np.arange(bs)
+    p1, p2 = f32(pool), f32(pool)
+    zd = bf(zbig)[:, :HV * D].view(bs, HV, D)           # strided rows, as a projection slice
+    fused = ops.recurrent_gdn_inplace(bf(q), bf(k), bf(v), f32(g), bf(beta), p1, i64(ids),
+                                      z=zd, norm_weight=bf(w), eps=1e-6)
+    plain = ops.recurrent_gdn_inplace(bf(q), bf(k), bf(v), f32(g), bf(beta), p2, i64(ids))
+    ref = ops.rms_norm_gated(plain[:, 0], zd, bf(w), 1e-6)
+    assert torch.equal(p1, p2)
+    assert_bf16_close(host(fused)[:, 0], host(ref), ulps=1, atol=1e-3)
+
+
+def test_chunk_fused_norm(ops):
+    for D, HK, HV in ((128, 2, 4), (64, 2, 4)):          # tensor-core and fp32 kernels
+        lens = [70, 1, 130]
+        N = sum(lens)
+        q, k, v, g, beta = I.core_inputs(N, HK, D, HV, D, seed=63)
+        q, k, v, beta = (O.round_bf16(t) for t in (q, k, v, beta))
+        r = I.rng(64)
+        zbig = O.round_bf16(r.standard_normal((N, HV * D + 8)).astype(np.float32))
+        w = O.round_bf16((1 + 0.1 * r.standard_normal(D)).astype(np.float32))
+        cu = I.cu_from_lens(lens)
+        p1 = torch.zeros(3, HV, D, D, device=DEV)
+        p2 = p1.clone()
+        zd = bf(zbig)[:, :HV * D].view(N, HV, D)
+        fused = ops.chunk_gated_delta_rule_varlen(bf(q), bf(k), bf(v), f32(g), bf(beta), p1,
+                                                  i64([0, 1, 2]), i32(cu), max(lens), z=zd,
+                                                  norm_weight=bf(w), eps=1e-6)
+        plain = ops.chunk_gated_delta_rule_varlen(bf(q), bf(k), bf(v), f32(g), bf(beta), p2,
+                                                  i64([0, 1, 2]), i32(cu), max(lens))
+        ref = ops.rms_norm_gated(plain, zd, bf(w), 1e-6)
+        assert torch.equal(p1, p2)
+        assert_bf16_close(host(fused), host(ref), ulps=1, atol=1e-3)
