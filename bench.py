@@ -57,7 +57,8 @@ def parse():
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--prefill-steps", type=int, default=3)
     ap.add_argument("--profile-case", default=None,
-                    choices=["recurrent", "conv_decode", "conv_varlen", "chunk", "gbeta", "norm"],
+                    choices=["recurrent", "decode_fused", "conv_decode", "conv_varlen", "chunk",
+                             "gbeta", "norm"],
                     help="run a small single-kernel case for ncu (3 launches) and exit")
     return ap.parse_args()
 
@@ -505,6 +506,20 @@ def profile_case(pkg, name):
         beta = torch.rand(bs, HV, generator=g, device=dev).to(torch.bfloat16)
         ids = torch.randperm(bs + 1, generator=torch.Generator().manual_seed(0))[:bs].to(dev)
         fn = lambda: ops.recurrent_gdn_inplace(q, k, v, gg, beta, pool, ids)
+    elif name == "decode_fused":       # the one-launch decode core, 257-slot pools
+        W = C + HV * D + 2 * HV + 64
+        pool = torch.randn(bs + 1, HV, D, D, generator=g, device=dev) * 0.02
+        cpool = torch.randn(bs + 1, C, 3, generator=g, device=dev).to(torch.bfloat16)
+        proj = torch.randn(bs, W, generator=g, device=dev).to(torch.bfloat16)
+        w = (torch.rand(C, 4, generator=g, device=dev) - 0.5).to(torch.bfloat16)
+        al = torch.rand(HV, device=dev) - 0.5
+        dtb = torch.zeros(HV, device=dev)
+        nw = torch.ones(D, device=dev, dtype=torch.bfloat16)
+        ids = torch.randperm(bs + 1, generator=torch.Generator().manual_seed(0))[:bs].to(dev)
+        mixed, z = proj[:, :C], proj[:, C:C + HV * D].view(bs, HV, D)
+        b = proj[:, C + HV * D:C + HV * D + HV]
+        a = proj[:, C + HV * D + HV:C + HV * D + 2 * HV]
+        fn = lambda: ops.decode_fused(mixed, z, b, a, cpool, w, al, dtb, pool, ids, nw)
     elif name == "conv_decode":        # 4096 rows x 8192 channels
         n = 4096
         pool = torch.randn(n + 1, C, 3, generator=g, device=dev).to(torch.bfloat16)
@@ -611,8 +626,10 @@ def main():
                        "cuda_graph": True, "parallelism": f"dp{world} (independent sequences)"},
             "state_gbs": round(world * state_bytes_step * args.steps / t / 1e9, 1),
             "e2e": e2e, "roofline": roof,
-            # per layer: gate, conv step, recurrent (+ fused gated norm)
-            "gpu_launches": 3 * c["layers"] * args.steps,
+            # per layer: the fused decode core (1 launch), or gate, conv step and
+            # recurrent with the gated norm fused (3 launches)
+            "gpu_launches": (1 if pkg.ops.decode_fused_preferred(c["bs"], c["HK"], dev)
+                             else 3) * c["layers"] * args.steps,
             "clocks": clk}
 
     if rank == 0 and world == 1 and not args.no_prefill:

@@ -38,7 +38,7 @@
 extern "C" {
 #endif
 
-#define GDN_ABI_VERSION 2
+#define GDN_ABI_VERSION 3
 
 enum gdn_status_code {
   GDN_OK = 0,
@@ -189,6 +189,38 @@ int gdn_chunk_prefill_varlen(const void* q, int64_t q_row_stride,
 int gdn_rms_norm_gated(const void* x, const void* gate, int64_t gate_token_stride,
                        int32_t heads_per_token, const void* weight, void* y,
                        int64_t n_rows, int32_t dim, float eps, void* stream);
+
+/*
+ * The whole decode core of one layer in one launch: conv step + g/beta gate +
+ * in-place recurrence + gated RMSNorm for bs decode rows, from the fused input
+ * projection outputs.  Replaces the decode branch of Qwen3_5GatedDeltaNet.forward
+ * (qwen3_5.py:1008-1026: conv_decode_step, fused_g_beta, recurrent_gdn_inplace;
+ * and :1083-1085: self.norm(core, z)), i.e. the sequence gdn_conv_decode_step +
+ * gdn_fused_g_beta + gdn_recurrent_inplace with the fused norm, whose results it
+ * reproduces bit for bit.  The reference has no single counterpart.
+ * mixed: bf16 rows [q | k | v] of conv_dim = (2*num_k_heads + num_v_heads) *
+ * head_dim channels (row stride mixed_row_stride); z: bf16 rows of
+ * num_v_heads*head_dim (z_row_stride); b, a: bf16 rows of num_v_heads
+ * (ab_row_stride).  conv_pool / conv_weight as gdn_conv_decode_step (channels =
+ * conv_dim, kernel = conv_kernel), rolled in place; a_log, dt_bias as
+ * gdn_fused_g_beta; s_pool as gdn_recurrent_inplace (head_k_dim = head_v_dim =
+ * head_dim); both pools are indexed by the same ids with num_slots slots.
+ * out: bf16 [bs, num_v_heads, head_dim] contiguous, the normed core output.
+ * Supported: head_dim 64 or 128, num_v_heads / num_k_heads <= 4, conv_kernel
+ * 2..4; s_pool 16-byte aligned; mixed rows, conv slots and conv weight 4-byte
+ * aligned (even strides).  A row whose slot id is out of range is skipped
+ * (GDN_STATUS_BAD_SLOT), its out rows are left unwritten.
+ */
+int gdn_decode_fused(const void* mixed, int64_t mixed_row_stride,
+                     const void* z, int64_t z_row_stride,
+                     const void* b, const void* a, int64_t ab_row_stride,
+                     void* conv_pool, int64_t conv_slot_stride,
+                     const void* conv_weight, int32_t conv_kernel,
+                     const void* a_log, const void* dt_bias, int32_t param_dtype,
+                     float* s_pool, int64_t slot_stride, int64_t num_slots,
+                     const int64_t* ids, const void* norm_weight, float norm_eps,
+                     void* out, int32_t bs, int32_t num_k_heads, int32_t num_v_heads,
+                     int32_t head_dim, float scale, int32_t* status, void* stream);
 
 #ifdef __cplusplus
 }

@@ -61,6 +61,33 @@ __device__ __forceinline__ float gated_norm_elem(float x, float inv, float w, fl
   return u * siluf_(z);
 }
 
+// Depthwise conv tap sum + SiLU for one channel: acc = sum_{i<K} w[i] *
+// win[i] in tap order, win[K-1] the current input (qwen3_5.py:438-446,
+// 540-548); SiLU with the hardware exp2 / reciprocal approximations (a few
+// fp32 ulps before the bf16 rounding of the result).  Every conv path uses
+// this function, so a token's value does not depend on the kernel that
+// computed it.
+__device__ __forceinline__ float conv_silu(float a) { return __fdividef(a, 1.0f + __expf(-a)); }
+
+template <int K>
+__device__ __forceinline__ float conv_point(const float* win, const float* w) {
+  float a = win[0] * w[0];
+#pragma unroll
+  for (int i = 1; i < K; ++i) a = fmaf(win[i], w[i], a);
+  return conv_silu(a);
+}
+
+// The decay gate and write strength of one (token, v-head) (qwen3_5.py:320-343):
+// g = -exp(A_log) * softplus(a + dt_bias) (softplus threshold 20), beta =
+// sigmoid(b) rounded to bf16 (the reference stores beta in the model dtype).
+__device__ __forceinline__ void gate_value(float av, float bv, float a_log, float dt_bias,
+                                           float& g, float& beta) {
+  const float z = av + dt_bias;
+  const float sp = z > 20.0f ? z : logf(1.0f + expf(z));
+  g = -expf(a_log) * sp;
+  beta = round_bf(sigmoidf_(bv));
+}
+
 // 8 packed bf16 <-> 8 floats
 __device__ __forceinline__ void unpack8(const uint4& u, float* f) {
   const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);

@@ -17,12 +17,24 @@
 // state to its last K-1 inputs.  A single launch would let the CTA holding a
 // sequence's tail overwrite the state before the CTA holding its head has
 // read it.
+//
+// The prefill is HBM-bound (2 bytes in + 2 bytes out per element; the K-1 halo
+// rows a tile re-reads come from L2).  A tile whose K-1 halo rows and all of
+// whose tokens lie inside one sequence (all but a few tiles per sequence)
+// copies its K-1+16 rows into shared memory with cp.async at once (each
+// thread its own 16-byte column, ~300 bytes in flight per thread without
+// holding registers); tiles at sequence boundaries take the general
+// per-token path.  Both
+// paths evaluate one output with the same conv_point(), so a token's value
+// does not depend on where its tile starts (split prefills match one-shot
+// prefills bit for bit).
 #include "common.cuh"
+#include "tc_util.cuh"
 
 namespace gdn {
 
 constexpr int kConvThreads = 128;  // 128 threads x 8 channels = 1024 channels per CTA
-constexpr int kConvTileTokens = 32;
+constexpr int kConvTileTokens = 16;
 
 // ---------------------------------------------------------------------------
 // single-token decode step: qwen3_5.py:515-558
@@ -51,10 +63,11 @@ __global__ void __launch_bounds__(kConvThreads) conv_decode_vec_kernel(
   for (int j = 0; j < K; ++j) unpack8(wp[j], wv + 8 * j);
 #pragma unroll
   for (int ch = 0; ch < 8; ++ch) {
-    float a = xv[ch] * wv[ch * K + (K - 1)];
+    float win[K];
 #pragma unroll
-    for (int i = 0; i < T; ++i) a += sv[ch * T + i] * wv[ch * K + i];
-    acc[ch] = siluf_(a);
+    for (int i = 0; i < T; ++i) win[i] = sv[ch * T + i];
+    win[T] = xv[ch];
+    acc[ch] = conv_point<K>(win, wv + ch * K);
   }
   *reinterpret_cast<uint4*>(y + n * ys + c0) = pack8(acc);
   // roll: [s1 .. s_{T-1}, x]  (bit copies of bf16 values)
@@ -82,13 +95,13 @@ __global__ void __launch_bounds__(kConvThreads) conv_decode_scalar_kernel(
   constexpr int T = K - 1;
   bf16* sp = pool + slot * slot_stride + (int64_t)c * T;
   const bf16 xb = x[n * xs + c];
-  float s[T];
+  float win[K], wv[K];
 #pragma unroll
-  for (int i = 0; i < T; ++i) s[i] = bf2f(sp[i]);
-  float a = bf2f(xb) * bf2f(w[(int64_t)c * K + K - 1]);
+  for (int i = 0; i < T; ++i) win[i] = bf2f(sp[i]);
+  win[T] = bf2f(xb);
 #pragma unroll
-  for (int i = 0; i < T; ++i) a += s[i] * bf2f(w[(int64_t)c * K + i]);
-  y[n * ys + c] = f2bf(siluf_(a));
+  for (int i = 0; i < K; ++i) wv[i] = bf2f(w[(int64_t)c * K + i]);
+  y[n * ys + c] = f2bf(conv_point<K>(win, wv));
 #pragma unroll
   for (int i = 0; i + 1 < T; ++i) sp[i] = sp[i + 1];
   sp[T - 1] = xb;
@@ -136,6 +149,45 @@ __global__ void __launch_bounds__(kConvThreads) conv_varlen_kernel(
   while (t_begin >= seq_end && r + 1 < n_seqs) {  // skip empty sequences
     ++r; seq_start = cu[r]; seq_end = cu[r + 1];
   }
+
+  if constexpr (VEC) {
+    constexpr int TT = kConvTileTokens;
+    // [row][thread]: a warp's 32 columns of one row are 512 contiguous bytes
+    __shared__ uint4 tile[T + TT][kConvThreads];
+    // Interior tile: rows t_begin-T .. t_begin+TT-1 all belong to sequence r.
+    if (t_begin - T >= seq_start && t_begin >= T && t_begin + TT <= seq_end &&
+        seq_end <= n_tokens) {
+      const bf16* xp = x + (t_begin - T) * xs + c0;
+#pragma unroll
+      for (int i = 0; i < T + TT; ++i)
+        tc::cp_async16(tc::smem_u32(&tile[i][threadIdx.x]), xp + i * xs, 16);
+      tc::cp_async_commit();
+      tc::cp_async_wait<0>();  // each thread reads back only its own column
+      float win[K][8];  // win[j][ch]: input at t-T+j
+#pragma unroll
+      for (int j = 0; j < T; ++j) unpack8(tile[j][threadIdx.x], win[j]);
+      bf16* yp = y + t_begin * ys + c0;
+#pragma unroll
+      for (int i = 0; i < TT; ++i) {
+        unpack8(tile[T + i][threadIdx.x], win[T]);
+        float out[8];
+#pragma unroll
+        for (int ch = 0; ch < 8; ++ch) {
+          float wn[K];
+#pragma unroll
+          for (int j = 0; j < K; ++j) wn[j] = win[j][ch];
+          out[ch] = conv_point<K>(wn, wv + ch * K);
+        }
+        __stcs(reinterpret_cast<uint4*>(yp + i * ys), pack8(out));
+#pragma unroll
+        for (int j = 0; j < T; ++j)
+#pragma unroll
+          for (int ch = 0; ch < 8; ++ch) win[j][ch] = win[j + 1][ch];
+      }
+      return;
+    }
+  }
+
   float win[T][V];  // win[j] = input at position t-T+j
   bool need_init = true;
   for (int64_t t = t_begin; t < t_end; ++t) {
@@ -172,11 +224,11 @@ __global__ void __launch_bounds__(kConvThreads) conv_varlen_kernel(
     float out[V];
 #pragma unroll
     for (int ch = 0; ch < V; ++ch) {
-      float a = 0.f;
+      float wn[K];
 #pragma unroll
-      for (int i = 0; i < T; ++i) a += win[i][ch] * wv[ch * K + i];
-      a += xv[ch] * wv[ch * K + T];
-      out[ch] = siluf_(a);
+      for (int i = 0; i < T; ++i) wn[i] = win[i][ch];
+      wn[T] = xv[ch];
+      out[ch] = conv_point<K>(wn, wv + ch * K);
     }
     if constexpr (VEC) *reinterpret_cast<uint4*>(y + t * ys + c0) = pack8(out);
     else y[t * ys + c0] = f2bf(out[0]);

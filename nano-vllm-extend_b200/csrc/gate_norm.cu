@@ -27,14 +27,12 @@ __global__ void __launch_bounds__(256) gbeta_kernel(
        i += (int64_t)gridDim.x * blockDim.x) {
     const int64_t r = i / H;
     const int h = (int)(i - r * H);
-    const float av = bf2f(a[r * row_stride + h]);
-    const float bv = bf2f(b[r * row_stride + h]);
-    const float z = av + load_param<P>(dt_bias, h);
-    const float sp = z > 20.0f ? z : logf(1.0f + expf(z));
-    float gv = -expf(load_param<P>(a_log, h)) * sp;
+    float gv, bt;
+    gate_value(bf2f(a[r * row_stride + h]), bf2f(b[r * row_stride + h]),
+               load_param<P>(a_log, h), load_param<P>(dt_bias, h), gv, bt);
     if (mask != nullptr && mask[r] == 0) gv = 0.0f;
     g[i] = gv;
-    beta[i] = f2bf(sigmoidf_(bv));
+    beta[i] = f2bf(bt);
   }
 }
 

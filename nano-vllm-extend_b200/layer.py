@@ -55,6 +55,12 @@ class Qwen3_5GatedDeltaNet(nn.Module):
     installed); ``get_context`` returns the per-step Context.
     """
 
+    # Decode rows through the one-launch fused core (ops.decode_fused): None
+    # picks it where it is the faster route (ops.decode_fused_preferred),
+    # True whenever the shape allows, False never (the four operators; the
+    # results are identical).
+    fused_decode = None
+
     def __init__(self, config, parallel=None, get_context=None) -> None:
         super().__init__()
         P = parallel if parallel is not None else _parallel
@@ -156,8 +162,6 @@ class Qwen3_5GatedDeltaNet(nn.Module):
         z = proj[:, r[0]:r[1]].view(N, hv, self.head_v_dim)
         b = proj[:, r[1]:r[2]]
         a = proj[:, r[2]:r[3]]
-        g, beta = ops.fused_g_beta(b, a, self.A_log[self._v_head_slice],
-                                   self.dt_bias[self._v_head_slice], None)
 
         T = int(ctx.max_seqlen_q)
         if T == 1:
@@ -169,14 +173,16 @@ class Qwen3_5GatedDeltaNet(nn.Module):
             n1 = 0
             while n1 < len(lens_q) and lens_q[n1] == 1:
                 n1 += 1
-        # the gated RMSNorm (self.norm) runs fused in each core kernel's epilogue
+        # the gated RMSNorm (self.norm) runs fused in each core's kernels
         outs = []
         if n1:
-            outs.append(self._decode_core(mixed[:n1], g[:n1], beta[:n1], ids[:n1], z[:n1]))
+            outs.append(self._decode_core(mixed[:n1], z[:n1], b[:n1], a[:n1], ids[:n1]))
         if n1 < N:
             cu_q = ctx.cu_seqlens_q
             cu_p = cu_q[n1:] - cu_q[n1] if n1 else cu_q
-            outs.append(self._prefill_core(mixed[n1:], g[n1:], beta[n1:], ids[n1:], cu_p,
+            g, beta = ops.fused_g_beta(b[n1:], a[n1:], self.A_log[self._v_head_slice],
+                                       self.dt_bias[self._v_head_slice], None)
+            outs.append(self._prefill_core(mixed[n1:], g, beta, ids[n1:], cu_p,
                                            max(lens_q[n1:]), z[n1:]))
         core = outs[0] if len(outs) == 1 else torch.cat(outs, 0)    # [N, HV, DV], normed
         return self.out_proj(core.view(N, vd))
@@ -189,11 +195,22 @@ class Qwen3_5GatedDeltaNet(nn.Module):
         v = y[:, 2 * kd:].view(n, self.num_v_heads, self.head_v_dim)
         return q, k, v
 
-    def _decode_core(self, mixed, g, beta, ids, z):
-        """T == 1 rows: conv step + in-place recurrent + gated norm
-        (qwen3_5.py:1008-1026, 1083-1085)."""
-        y = ops.conv_decode_step(mixed, self.conv_cache, ids,
-                                 self.conv1d.weight.view(self.conv_dim, self.conv_kernel))
+    def _decode_core(self, mixed, z, b, a, ids):
+        """T == 1 rows: conv step + gate + in-place recurrent + gated norm
+        (qwen3_5.py:976-982, 1008-1026, 1083-1085), one fused kernel when the
+        shape allows (``fused_decode``), else the four operators."""
+        a_log = self.A_log[self._v_head_slice]
+        dt_bias = self.dt_bias[self._v_head_slice]
+        w = self.conv1d.weight.view(self.conv_dim, self.conv_kernel)
+        use = self.fused_decode
+        if use is None:
+            use = ops.decode_fused_preferred(mixed.shape[0], self.num_k_heads, mixed.device)
+        if use and ops.decode_fused_supported(self.num_k_heads, self.num_v_heads,
+                                              self.head_k_dim, self.head_v_dim, self.conv_kernel):
+            return ops.decode_fused(mixed, z, b, a, self.conv_cache, w, a_log, dt_bias,
+                                    self.s_cache, ids, self.norm.weight, self.norm.eps)
+        g, beta = ops.fused_g_beta(b, a, a_log, dt_bias, None)
+        y = ops.conv_decode_step(mixed, self.conv_cache, ids, w)
         q, k, v = self._split(y)
         o = ops.recurrent_gdn_inplace(q, k, v, g, beta, self.s_cache, ids, z=z,
                                       norm_weight=self.norm.weight, eps=self.norm.eps)

@@ -32,7 +32,10 @@ def status_word(device) -> torch.Tensor:
     idx = device.index if device.index is not None else torch.cuda.current_device()
     t = _STATUS.get(idx)
     if t is None:
-        t = torch.zeros(1, dtype=torch.int32, device=torch.device("cuda", idx))
+        # a normal tensor even when first made under inference_mode, so that
+        # check_status can clear it anywhere
+        with torch.inference_mode(False):
+            t = torch.zeros(1, dtype=torch.int32, device=torch.device("cuda", idx))
         _STATUS[idx] = t
     return t
 
@@ -317,3 +320,81 @@ def rms_norm_gated(x: torch.Tensor, gate: torch.Tensor, weight: torch.Tensor,
         _stream_ptr(x.device))
     _lib.check(rc, "gdn_rms_norm_gated")
     return y
+
+
+# ---------------------------------------------------------------------------
+# the fused decode core (conv step + gate + recurrence + gated norm)
+# ---------------------------------------------------------------------------
+
+
+def decode_fused_supported(num_k_heads: int, num_v_heads: int, head_k_dim: int,
+                           head_v_dim: int, conv_kernel: int) -> bool:
+    """Whether :func:`decode_fused` serves this layer shape."""
+    return (head_k_dim == head_v_dim and head_k_dim in (64, 128) and
+            num_v_heads % num_k_heads == 0 and num_v_heads // num_k_heads <= 4 and
+            2 <= conv_kernel <= 4)
+
+
+_SM_COUNT: dict[int, int] = {}
+
+
+def decode_fused_preferred(bs: int, num_k_heads: int, device) -> bool:
+    """Whether the fused decode core beats the four-operator sequence for bs
+    rows: it does while the k-head groups (bs * num_k_heads, one CTA's work
+    item) number at most 4 per SM; above that the four-operator sequence's
+    register-resident recurrent kernel streams the state faster."""
+    device = torch.device(device)
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    n = _SM_COUNT.get(idx)
+    if n is None:
+        n = torch.cuda.get_device_properties(idx).multi_processor_count
+        _SM_COUNT[idx] = n
+    return bs * num_k_heads <= 4 * n
+
+
+def decode_fused(mixed: torch.Tensor, z: torch.Tensor, b: torch.Tensor, a: torch.Tensor,
+                 conv_pool: torch.Tensor, conv_weight: torch.Tensor, a_log: torch.Tensor,
+                 dt_bias: torch.Tensor, s_pool: torch.Tensor, ids: torch.Tensor,
+                 norm_weight: torch.Tensor, eps: float = 1e-6) -> torch.Tensor:
+    """The decode branch of Qwen3_5GatedDeltaNet.forward for T == 1 rows in one
+    kernel: conv_decode_step (qwen3_5.py:1008-1012) + fused_g_beta (:976-982)
+    + recurrent_gdn_inplace (:1013-1026) + the gated norm (:1083-1085).
+    mixed [bs, conv_dim] (the [q | k | v] columns of the projection, rows may
+    be strided), z [bs, HV, D] (token stride may exceed HV*D), b / a [bs, HV]
+    (shared row stride); conv_pool [slots, conv_dim, K-1] and s_pool [slots,
+    HV, D, D] per-layer views rolled / updated in place at rows ``ids``.
+    Returns the normed core output [bs, HV, D] (bit-identical to the
+    four-operator sequence)."""
+    _cuda(mixed, z, b, a, conv_pool, conv_weight, a_log, dt_bias, s_pool, ids, norm_weight)
+    bs = mixed.shape[0]
+    HV, DK, DV = s_pool.shape[1], s_pool.shape[2], s_pool.shape[3]
+    D = DV
+    C = mixed.shape[-1]
+    assert DK == DV, "decode_fused needs head_k_dim == head_v_dim"
+    assert (C // D - HV) % 2 == 0 and C % D == 0, "mixed must hold [q | k | v] of whole heads"
+    HK = (C // D - HV) // 2
+    w = conv_weight.reshape(C, -1).contiguous()
+    K = w.shape[1]
+    _pool_view_check(conv_pool, K - 1, C)
+    _state_view_check(s_pool, HV, D, D)
+    assert mixed.dtype == torch.bfloat16 and w.dtype == torch.bfloat16
+    m2, ms = _rows2d(mixed, C)
+    assert m2.shape[0] == bs
+    z3, zs, nw = _norm_args(z, norm_weight, bs, HV, D)
+    assert b.shape == (bs, HV) and a.shape == (bs, HV) and b.stride(1) == 1 and \
+        a.stride(1) == 1 and a.stride(0) == b.stride(0), "b / a must share a row stride"
+    assert b.dtype == torch.bfloat16 and a.dtype == torch.bfloat16
+    assert a_log.dtype == dt_bias.dtype and a_log.dtype in (torch.float32, torch.bfloat16)
+    assert a_log.numel() == HV and dt_bias.numel() == HV
+    pdt = _lib.GDN_DTYPE_F32 if a_log.dtype == torch.float32 else _lib.GDN_DTYPE_BF16
+    ids = _ids64(ids)
+    assert ids.numel() == bs
+    assert conv_pool.shape[0] == s_pool.shape[0], "both pools index the same slots"
+    out = torch.empty(bs, HV, D, dtype=torch.bfloat16, device=mixed.device)
+    rc = _lib.load().gdn_decode_fused(
+        _p(m2), ms, _p(z3), zs, _p(b), _p(a), b.stride(0), _p(conv_pool), _slot_stride(conv_pool),
+        _p(w), K, _p(a_log.contiguous()), _p(dt_bias.contiguous()), pdt, _p(s_pool),
+        _slot_stride(s_pool), s_pool.shape[0], _p(ids), _p(nw), float(eps), _p(out), bs, HK, HV,
+        D, D ** -0.5, _p(status_word(mixed.device)), _stream_ptr(mixed.device))
+    _lib.check(rc, "gdn_decode_fused")
+    return out

@@ -21,7 +21,7 @@ def test_header_declares_the_path():
     syms = declared_symbols()
     for s in ("gdn_fused_g_beta", "gdn_conv_decode_step", "gdn_causal_conv_silu_varlen",
               "gdn_recurrent_inplace", "gdn_chunk_prefill_varlen", "gdn_rms_norm_gated",
-              "gdn_abi_version", "gdn_last_error"):
+              "gdn_decode_fused", "gdn_abi_version", "gdn_last_error"):
         assert s in syms
 
 
@@ -104,3 +104,43 @@ def test_python_errors_map_from_codes(pkg):
         L.check(L.GDN_ERR_UNSUPPORTED, "x")
     with pytest.raises(RuntimeError):
         L.check(L.GDN_ERR_CUDA, "x")
+
+
+def _decode_fused_args(**kw):
+    """gdn_decode_fused arguments for a bs-1 call of HK=2, HV=4, D=128, K=4
+    with null pointers (host checks only), overridable by name."""
+    a = dict(mixed=None, ms=8192, z=None, zs=4096, b=None, a=None, abs_=8, conv_pool=None,
+             conv_ss=8192 * 3, conv_w=None, K=4, a_log=None, dt_bias=None, pdt=0, s_pool=None,
+             slot_stride=4 * 128 * 128, num_slots=2, ids=None, nw=None, eps=1e-6, out=None, bs=1,
+             HK=2, HV=4, D=128, scale=0.1, status=None, stream=None)
+    a.update(kw)
+    return list(a.values())
+
+
+def test_decode_fused_host_validation(pkg):
+    L = pkg._lib
+    rc, msg = _call(pkg, "gdn_decode_fused", *_decode_fused_args(D=96))
+    assert rc == L.GDN_ERR_UNSUPPORTED and "head dim" in msg
+    rc, msg = _call(pkg, "gdn_decode_fused", *_decode_fused_args(HK=1, HV=8, zs=8192,
+                                                                  ms=10 * 128,
+                                                                  conv_ss=10 * 128 * 3,
+                                                                  slot_stride=8 * 128 * 128))
+    assert rc == L.GDN_ERR_UNSUPPORTED and "v-heads per k-head" in msg
+    rc, msg = _call(pkg, "gdn_decode_fused", *_decode_fused_args(HV=3))
+    assert rc == L.GDN_ERR_INVALID_ARGUMENT and "multiple" in msg
+    rc, msg = _call(pkg, "gdn_decode_fused", *_decode_fused_args(K=5))
+    assert rc == L.GDN_ERR_UNSUPPORTED and "conv kernel" in msg
+    rc, msg = _call(pkg, "gdn_decode_fused", *_decode_fused_args(pdt=7))
+    assert rc == L.GDN_ERR_INVALID_ARGUMENT and "param_dtype" in msg
+    rc, msg = _call(pkg, "gdn_decode_fused", *_decode_fused_args(slot_stride=1000))
+    assert rc == L.GDN_ERR_INVALID_ARGUMENT and "slot_stride" in msg
+    rc, msg = _call(pkg, "gdn_decode_fused", *_decode_fused_args(conv_ss=100))
+    assert rc == L.GDN_ERR_INVALID_ARGUMENT and "conv_slot_stride" in msg
+    rc, msg = _call(pkg, "gdn_decode_fused", *_decode_fused_args(ms=100))
+    assert rc == L.GDN_ERR_INVALID_ARGUMENT and "row stride" in msg
+    # zero rows: nothing to do, no pointer is touched
+    rc, msg = _call(pkg, "gdn_decode_fused", *_decode_fused_args(bs=0))
+    assert rc == L.GDN_OK
+    # rows with null pointers are rejected before any launch
+    rc, msg = _call(pkg, "gdn_decode_fused", *_decode_fused_args())
+    assert rc == L.GDN_ERR_INVALID_ARGUMENT and "null" in msg
