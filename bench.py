@@ -224,46 +224,62 @@ def time_region(fn, steps, world, stream=None):
     return max_over_ranks(e0.elapsed_time(e1) / 1e3, world)
 
 
-def recurrent_kernel_roofline(pkg, stack, peaks, launches):
-    """Time the in-place recurrent kernel alone (one launch per layer view,
-    each on its own 1 GB of state) with CUDA events on its stream."""
+def decode_kernel_roofline(pkg, stack, peaks, launches):
+    """Time the fused decode-core kernel alone as the layer launches it (one
+    launch per layer, each on its own layer views of the stack's 38.7 GB state
+    and conv pools) with CUDA events on its stream."""
     ops = pkg.ops
     c = C1
-    bs, HK, HV, D = c["bs"], c["HK"], c["HV"], c["DK"]
+    bs, HK, HV, D, K = c["bs"], c["HK"], c["HV"], c["DK"], c["K"]
+    m0 = stack.layers[0]
     g = torch.Generator(device=stack.dev).manual_seed(7)
-    mixed = torch.randn(bs, 2 * HK * D + HV * D, generator=g, device=stack.dev).to(torch.bfloat16)
-    q = mixed[:, :HK * D].view(bs, HK, D)
-    k = mixed[:, HK * D:2 * HK * D].view(bs, HK, D)
-    v = mixed[:, 2 * HK * D:].view(bs, HV, D)
-    gg = -torch.rand(bs, HV, generator=g, device=stack.dev)
-    beta = torch.rand(bs, HV, generator=g, device=stack.dev).to(torch.bfloat16)
-    views = [m.s_cache for m in stack.layers]
-    # as the layer calls it: gated-RMSNorm epilogue fused (z read, normed output)
-    z = torch.randn(bs, HV, D, generator=g, device=stack.dev).to(torch.bfloat16)
-    nw = torch.ones(D, device=stack.dev, dtype=torch.bfloat16)
-    for vw in views[:3]:
-        ops.recurrent_gdn_inplace(q, k, v, gg, beta, vw, stack.ids, z=z, norm_weight=nw)
-    torch.cuda.synchronize()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    n = 0
-    e0.record()
-    for _ in range(launches):
-        for vw in views:
-            ops.recurrent_gdn_inplace(q, k, v, gg, beta, vw, stack.ids, z=z, norm_weight=nw)
-            n += 1
-    e1.record()
-    torch.cuda.synchronize()
+    C = m0.conv_dim
+    W = m0._fused_weight().shape[0]
+    proj = torch.randn(bs, W, generator=g, device=stack.dev).to(torch.bfloat16)
+    r = m0._proj_rows
+    mixed, z = proj[:, :C], proj[:, r[0]:r[1]].view(bs, HV, D)
+    b, a = proj[:, r[1]:r[2]], proj[:, r[2]:r[3]]
+
+    def launch(m):
+        return ops.decode_fused(mixed, z, b, a, m.conv_cache,
+                                m.conv1d.weight.view(m.conv_dim, m.conv_kernel), m.A_log,
+                                m.dt_bias, m.s_cache, stack.ids, m.norm.weight, m.norm.eps)
+
+    with torch.inference_mode():
+        for m in stack.layers[:3]:
+            launch(m)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        n = 0
+        e0.record()
+        for _ in range(launches):
+            for m in stack.layers:
+                launch(m)
+                n += 1
+        e1.record()
+        torch.cuda.synchronize()
     dt = e0.elapsed_time(e1) / 1e3 / n
-    state_bytes = 2 * bs * HV * D * D * 4
-    act_bytes = bs * (2 * HK * D + HV * D) * 2 + bs * HV * (4 + 2) + 2 * bs * HV * D * 2
-    algo = state_bytes + act_bytes
+    algo = decode_algorithmic_bytes(bs, HK, HV, D, K)
     achieved = algo / dt / 1e9
-    traffic = read_profile_traffic("recurrent_decode_c1.md")
-    return {"kernel": "recurrent_inplace_kernel", "bound": "hbm", "achieved": round(achieved, 1),
+    traffic = read_profile_traffic("decode_fused_c1.md")
+    return {"kernel": "decode_fused_kernel", "bound": "hbm", "achieved": round(achieved, 1),
             "peak": peaks["hbm_gbs"], "peak_source": peaks["source"], "unit": "GB/s",
             "frac": round(achieved / peaks["hbm_gbs"], 4),
             "traffic": traffic, "algorithmic_bytes_per_launch": algo,
             "launch_us": round(dt * 1e6, 2), "launches_timed": n}
+
+
+def decode_algorithmic_bytes(bs, HK, HV, D, K):
+    """Bytes one fused decode launch must move: each (row, v-head) state read
+    and written once (fp32), each conv state read and written once, the
+    projection inputs read (q/k/v channels, z, a, b), the output written, the
+    conv weight and slot ids read."""
+    C = (2 * HK + HV) * D
+    state = 2 * bs * HV * D * D * 4
+    conv_state = 2 * bs * C * (K - 1) * 2
+    inputs = bs * (C + HV * D + 2 * HV) * 2
+    out = bs * HV * D * 2
+    return state + conv_state + inputs + out + C * K * 2 + bs * 8
 
 
 def read_profile_traffic(name):
@@ -610,7 +626,7 @@ def main():
            "h2d_bytes_per_step": h_in.numel() * h_in.element_size(),
            "d2h_bytes_per_step": h_out.numel() * h_out.element_size()}
 
-    roof = recurrent_kernel_roofline(pkg, stack, peaks, launches=max(2, args.steps // 10))
+    roof = decode_kernel_roofline(pkg, stack, peaks, launches=max(2, args.steps // 10))
     state_bytes_step = c["layers"] * 2 * c["bs"] * c["HV"] * c["DK"] * c["DV"] * 4
 
     line = {"metric": "GDN decode tok/s (config 1: 18-layer stack, bs 256)",
@@ -628,8 +644,7 @@ def main():
             "e2e": e2e, "roofline": roof,
             # per layer: the fused decode core (1 launch), or gate, conv step and
             # recurrent with the gated norm fused (3 launches)
-            "gpu_launches": (1 if pkg.ops.decode_fused_preferred(c["bs"], c["HK"], dev)
-                             else 3) * c["layers"] * args.steps,
+            "gpu_launches": (1 if stack.layers[0].fused_decode else 3) * c["layers"] * args.steps,
             "clocks": clk}
 
     if rank == 0 and world == 1 and not args.no_prefill:

@@ -39,6 +39,7 @@
 #include <cuda.h>
 
 #include "tc_util.cuh"
+#include "tmap.cuh"
 
 namespace gdn {
 namespace tc {
@@ -623,24 +624,6 @@ bool chunk_tc_supported(int D, const void* q, int64_t qs, const void* k, int64_t
                         int64_t slot_stride, const void*, int64_t, const void*) {
   return D == tc::kD && aligned16(q) && aligned16(k) && aligned16(v) && aligned16(out) &&
          aligned16(pool) && qs % 8 == 0 && ks % 8 == 0 && vs % 8 == 0 && slot_stride % 4 == 0;
-}
-
-typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
-                                  const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
-                                  const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
-                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-
-static EncodeTiledFn encode_tiled() {
-  static EncodeTiledFn fn = nullptr;
-  if (fn == nullptr) {
-    void* p = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
-            cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<EncodeTiledFn>(p);
-  }
-  return fn;
 }
 
 // bf16 [rows, cols] view with a row stride (elements), 64 x 64 boxes, 128B swizzle.

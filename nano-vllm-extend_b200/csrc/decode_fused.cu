@@ -10,22 +10,27 @@
 //   norm       : out = bf16(bf16(w * bf16(o * rsqrt(mean o^2 + eps))) * silu(z))
 // with the fp32 state read from and written back to its pool slot in place.
 //
-// Work unit and race freedom.  A CTA owns whole k-head groups (b, hk): the
+// Work items and race freedom.  A CTA owns whole k-head groups (b, hk): the
 // R = HV / HK v-heads that share q/k head hk.  The group's conv channels
 // (q and k of head hk, v of its R heads) are convolved and their conv state
-// rolled once, by that CTA, before its R recurrence units run, so no other CTA
+// rolled once, by that CTA, before its recurrence units run, so no other CTA
 // reads a conv state this one rewrites.
 //
-// HBM pipeline.  The kernel is persistent (one CTA per SM for D = 128) and
-// streams the per-head fp32 states (D x D, contiguous in the pool) through an
-// NSTAGE-deep ring of shared-memory buffers with 1-D bulk async copies that
-// complete on mbarriers: while a unit computes, the states of the next
-// NSTAGE-1 units are already on the way, so HBM always has reads in flight.
-// New states go back from registers with streaming 16-byte stores.  The
-// recurrence maths, its reduction order, the conv tap order and the gate and
-// norm formulas are those of conv_decode_step + fused_g_beta +
-// recurrent_inplace + rms_norm_gated, so the fused result is bit-identical
-// to that four-launch sequence.
+// HBM pipeline.  The kernel is persistent (2 CTAs per SM at D = 128, 4 at
+// D = 64; 16 warps per SM either way).  A recurrence unit is one 64-column
+// part of a head's D x D fp32 state; each CTA streams its units through a
+// 3-deep ring of shared-memory tiles loaded by TMA (a [D rows x 64 columns]
+// box of the per-layer pool view, completing on an mbarrier), so while a unit
+// computes, the next two are in flight.  New state columns go back from
+// registers with streaming stores.  The next group's conv inputs, gates and z
+// are fetched into registers while the current group runs.
+//
+// Bit-identical results.  Threads own rows r0 + RG*i of VW adjacent columns,
+// RG = 8: the column sums run in the row order of recurrent_inplace's
+// full-tile kernels, and the conv, gate and norm formulas are the same device
+// functions, so the output and the states equal conv_decode_step +
+// fused_g_beta + recurrent_inplace (gated norm fused) bit for bit wherever
+// that sequence runs its full-tile recurrent kernel.
 //
 // Every mbarrier wait is bounded: on time-out the CTA raises
 // GDN_STATUS_TIMEOUT, drains the copies it has in flight (bounded again) and
@@ -34,61 +39,100 @@
 
 #include "common.cuh"
 #include "tc_util.cuh"
+#include "tmap.cuh"
 
 namespace gdn {
 
 constexpr int kDecMaxR = 4;                // v-heads per k-head served
-constexpr int kDecMaxGroupsPerCta = 512;   // slot table of one CTA
+constexpr int kDecMaxGroupsPerCta = 256;   // slot table of one CTA
+constexpr int kDecPartCols = 64;           // state columns per recurrence unit
 constexpr uint32_t kDecSpin = 1u << 22;
 
 template <int D>
 struct DecCfg;
 template <>
 struct DecCfg<128> {
-  static constexpr int NT = 256, NSTAGE = 3, CTAS = 1;
+  static constexpr int NT = 256, VW = 2, NSTAGE = 3, CTAS = 2;
 };
 template <>
 struct DecCfg<64> {
-  static constexpr int NT = 128, NSTAGE = 6, CTAS = 2;
+  static constexpr int NT = 128, VW = 4, NSTAGE = 3, CTAS = 4;
 };
 
 template <int D>
 struct DecSmem {
   static constexpr int NT = DecCfg<D>::NT;
-  static constexpr int RG = NT / (D / 4);   // rows per pass
-  float state[DecCfg<D>::NSTAGE][D * D];    // the state ring (bulk-copy targets)
-  float red[RG][D];
-  float delta[D];
+  static constexpr int RG = NT / (kDecPartCols / DecCfg<D>::VW);   // rows per pass
+  float state[DecCfg<D>::NSTAGE][D * kDecPartCols];   // TMA boxes [D rows][64 cols]
+  float red[RG][kDecPartCols];
+  float delta[kDecPartCols];
   float q[D], k[D];
   float v[kDecMaxR][D];
+  float o[D];                       // the head's core output, before the norm
+  // k^ and q^ of the rows each thread owns (rows r0 + RG*i), contiguous per r0
+  __align__(16) float kn[RG][D / RG];
+  __align__(16) float qn[RG][D / RG];
   float gate_g[kDecMaxR], gate_b[kDecMaxR];
-  float norm[2];
   float wsum[NT / 32];
   int64_t slot[kDecMaxGroupsPerCta];
   uint64_t bar[DecCfg<D>::NSTAGE];
   int abort;
 };
 
+// A vector of VW fp32 state columns.
+template <int VW>
+struct Vec;
+template <>
+struct Vec<2> {
+  float2 v;
+  __device__ __forceinline__ float& operator[](int i) { return i == 0 ? v.x : v.y; }
+};
+template <>
+struct Vec<4> {
+  float4 v;
+  __device__ __forceinline__ float& operator[](int i) {
+    return i == 0 ? v.x : (i == 1 ? v.y : (i == 2 ? v.z : v.w));
+  }
+};
+
+// The next group's conv inputs, gate inputs and z, held in registers.
+template <int K>
+struct GroupIn {
+  uint32_t x[2];             // two channel pairs per thread at most
+  uint32_t taps[2][K - 1];
+  uint32_t w[2][K];
+  float z[kDecMaxR];         // column tid of each head's z (tid < D)
+  float av, bv, al, db;      // a, b, A_log, dt_bias of head tid (tid < R)
+};
+
 template <int D, int K>
 __global__ void __launch_bounds__(DecCfg<D>::NT, DecCfg<D>::CTAS) decode_fused_kernel(
-    const bf16* __restrict__ mixed, int64_t ms, const bf16* __restrict__ zp, int64_t zs,
-    const bf16* __restrict__ bp, const bf16* __restrict__ ap, int64_t abs_,
-    bf16* __restrict__ conv_pool, int64_t conv_ss, const bf16* __restrict__ conv_w,
-    const void* __restrict__ a_log, const void* __restrict__ dt_bias, int param_f32,
-    float* __restrict__ pool, int64_t slot_stride, int64_t num_slots,
-    const int64_t* __restrict__ ids, const bf16* __restrict__ nw, float eps,
-    bf16* __restrict__ out, int bs, int HK, int R, float scale, int32_t* status) {
+    const __grid_constant__ CUtensorMap tm_state, const bf16* __restrict__ mixed, int64_t ms,
+    const bf16* __restrict__ zp, int64_t zs, const bf16* __restrict__ bp,
+    const bf16* __restrict__ ap, int64_t abs_, bf16* __restrict__ conv_pool, int64_t conv_ss,
+    const bf16* __restrict__ conv_w, const void* __restrict__ a_log,
+    const void* __restrict__ dt_bias, int param_f32, float* __restrict__ pool,
+    int64_t slot_stride, int64_t num_slots, const int64_t* __restrict__ ids,
+    const bf16* __restrict__ nw, float eps, bf16* __restrict__ out, int bs, int HK, int R,
+    float scale, int32_t* status) {
   constexpr int NT = DecCfg<D>::NT;
+  constexpr int VW = DecCfg<D>::VW;
   constexpr int NSTAGE = DecCfg<D>::NSTAGE;
-  constexpr int CG = D / 4;         // threads across a state row (float4 each)
-  constexpr int RG = NT / CG;       // rows per pass
-  constexpr int RPT = D / RG;       // rows per thread
-  constexpr int T = K - 1;          // conv taps kept in the state
-  constexpr uint32_t kStateBytes = D * D * 4;
-  static_assert(D <= NT && NT % CG == 0 && D % RG == 0, "bad tiling");
+  constexpr int PARTS = D / kDecPartCols;
+  constexpr int CG = kDecPartCols / VW;   // threads across a part's row
+  constexpr int RG = NT / CG;             // rows per pass (8)
+  constexpr int RPT = D / RG;             // rows per thread
+  constexpr int T = K - 1;                // conv taps kept in the state
+  constexpr int MAXP = 2;                 // channel pairs per thread
+  constexpr uint32_t kUnitBytes = D * kDecPartCols * 4;
+  static_assert(RG == 8 && D <= NT && NT % CG == 0 && D % RG == 0, "bad tiling");
+  static_assert((2 + kDecMaxR) * D / 2 <= MAXP * NT, "channel pairs per thread");
 
-  extern __shared__ __align__(128) unsigned char dsmem[];
-  DecSmem<D>& sm = *reinterpret_cast<DecSmem<D>*>(dsmem);
+  extern __shared__ __align__(16) unsigned char dsmem[];
+  // TMA tiles want 128-byte aligned shared memory: round the base up (the
+  // launch reserves 128 bytes of slack)
+  DecSmem<D>& sm = *reinterpret_cast<DecSmem<D>*>(
+      dsmem + ((128u - (tc::smem_u32(dsmem) & 127u)) & 127u));
 
   const int tid = threadIdx.x;
   const int c4 = tid % CG;
@@ -97,7 +141,9 @@ __global__ void __launch_bounds__(DecCfg<D>::NT, DecCfg<D>::CTAS) decode_fused_k
   const int n_groups = bs * HK;
   const int my_groups =
       n_groups > (int)blockIdx.x ? (n_groups - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
-  const int n_units = my_groups * R;
+  const int units_per_group = R * PARTS;
+  const int n_units = my_groups * units_per_group;
+  const int64_t rows_per_slot = slot_stride / D;   // TMA row coordinate of a slot
 
   for (int i = tid; i < my_groups; i += NT) {
     const int G = blockIdx.x + i * gridDim.x;
@@ -110,18 +156,20 @@ __global__ void __launch_bounds__(DecCfg<D>::NT, DecCfg<D>::CTAS) decode_fused_k
   }
   __syncthreads();
 
-  // Producer (thread 0): queue unit u's state copy into stage u % NSTAGE; a
+  // Producer (thread 0): queue unit u's state tile into stage u % NSTAGE; a
   // unit whose slot is out of range completes the phase without a copy.
   auto issue = [&](int u) {
-    const int gi = u / R, j = u - gi * R;
+    const int gi = u / units_per_group;
+    const int rem = u - gi * units_per_group;
+    const int j = rem / PARTS, part = rem - j * PARTS;
     const int G = blockIdx.x + gi * gridDim.x;
     const int hk = G % HK;
     const int64_t slot = sm.slot[gi];
     const uint32_t bar = tc::smem_u32(&sm.bar[u % NSTAGE]);
     if (slot >= 0 && slot < num_slots) {
-      tc::mbar_expect_tx(bar, kStateBytes);
-      tc::bulk_load(tc::smem_u32(sm.state[u % NSTAGE]),
-                    pool + slot * slot_stride + (int64_t)(hk * R + j) * D * D, kStateBytes, bar);
+      tc::mbar_expect_tx(bar, kUnitBytes);
+      tc::tma_load_2d(tc::smem_u32(sm.state[u % NSTAGE]), &tm_state, part * kDecPartCols,
+                      (int)(slot * rows_per_slot + (int64_t)(hk * R + j) * D), bar);
     } else {
       tc::mbar_arrive(bar);
     }
@@ -129,8 +177,76 @@ __global__ void __launch_bounds__(DecCfg<D>::NT, DecCfg<D>::CTAS) decode_fused_k
   if (tid == 0)
     for (int u = 0; u < NSTAGE && u < n_units; ++u) issue(u);
 
+  // Fetch group gi's inputs into registers (plain loads, consumed a group later).
+  const int n_pairs = (2 + R) * D / 2;
+  auto fetch = [&](int gi, GroupIn<K>& in) {
+    const int G = blockIdx.x + gi * gridDim.x;
+    const int b = G / HK;
+    const int hk = G - b * HK;
+    const int64_t slot = sm.slot[gi];
+    if (!(slot >= 0 && slot < num_slots)) return;
+    const bf16* xrow = mixed + (int64_t)b * ms;
+#pragma unroll
+    for (int pi = 0; pi < MAXP; ++pi) {
+      const int p = tid + pi * NT;
+      if (p < n_pairs) {
+        const int c = 2 * p;
+        const int cg = c < D ? hk * D + c
+                             : (c < 2 * D ? HK * D + hk * D + (c - D)
+                                          : 2 * HK * D + hk * R * D + (c - 2 * D));
+        in.x[pi] = *reinterpret_cast<const uint32_t*>(xrow + cg);
+        const uint32_t* tp =
+            reinterpret_cast<const uint32_t*>(conv_pool + slot * conv_ss + (int64_t)cg * T);
+#pragma unroll
+        for (int i = 0; i < T; ++i) in.taps[pi][i] = tp[i];
+        const uint32_t* wp = reinterpret_cast<const uint32_t*>(conv_w + (int64_t)cg * K);
+#pragma unroll
+        for (int i = 0; i < K; ++i) in.w[pi][i] = wp[i];
+      }
+    }
+    if (tid < D) {
+#pragma unroll
+      for (int j = 0; j < kDecMaxR; ++j)
+        in.z[j] = j < R ? bf2f(zp[(int64_t)b * zs + (int64_t)(hk * R + j) * D + tid]) : 0.f;
+    }
+    if (tid < R) {
+      const int h = hk * R + tid;
+      in.av = bf2f(ap[(int64_t)b * abs_ + h]);
+      in.bv = bf2f(bp[(int64_t)b * abs_ + h]);
+      in.al = param_f32 ? reinterpret_cast<const float*>(a_log)[h]
+                        : bf2f(reinterpret_cast<const bf16*>(a_log)[h]);
+      in.db = param_f32 ? reinterpret_cast<const float*>(dt_bias)[h]
+                        : bf2f(reinterpret_cast<const bf16*>(dt_bias)[h]);
+    }
+  };
+
   const float wn = tid < D ? bf2f(nw[tid]) : 0.f;
+  const int lane = tid & 31;
+  GroupIn<K> cur;
+  if (my_groups > 0) fetch(0, cur);
   int consumed = 0;   // units whose stage has been waited for
+
+  // The gated RMSNorm of a finished head runs inside the next unit, on that
+  // unit's barriers: its sum of squares after the stage barrier, the scaled
+  // output after the first reduction barrier.  pend marks such a head, prow
+  // its output row, pz this thread's z value of it.
+  bool pend = false;
+  int64_t prow = 0;
+  float pz = 0.f;
+  auto norm_store = [&](float x, float inv) {
+    if (tid < D) out[prow * D + tid] = f2bf(gated_norm_elem(x, inv, wn, pz));
+  };
+  auto norm_sumsq = [&](float& x) {
+    x = tid < D ? round_bf(sm.o[tid]) : 0.f;   // the core output is bf16 first
+    const float ss = warp_sum(x * x);
+    if (lane == 0) sm.wsum[tid >> 5] = ss;
+  };
+  auto norm_inv = [&]() {
+    float tot = 0.f;
+#pragma unroll
+    for (int w = 0; w < NT / 32; ++w) tot += sm.wsum[w];
+    return rsqrtf(tot / (float)D + eps);
+  };
 
   for (int gi = 0; gi < my_groups; ++gi) {
     const int G = blockIdx.x + gi * gridDim.x;
@@ -140,168 +256,208 @@ __global__ void __launch_bounds__(DecCfg<D>::NT, DecCfg<D>::CTAS) decode_fused_k
     const bool valid = slot >= 0 && slot < num_slots;
     if (!valid && tid == 0 && status) atomicOr(status, GDN_STATUS_BAD_SLOT);
 
-    // ---- group prologue: conv step over q/k of head hk and v of its R heads,
-    // conv-state roll, gates of the R heads, z of this thread's column ----
+    // ---- group prologue: conv step over q/k of head hk and v of its R heads
+    // (from the prefetched registers), conv-state roll, gates ----
     float zv[kDecMaxR];
     if (valid) {
-      const bf16* xrow = mixed + (int64_t)b * ms;
-      if (tid < D) {
 #pragma unroll
-        for (int j = 0; j < kDecMaxR; ++j)
-          zv[j] = j < R ? bf2f(zp[(int64_t)b * zs + (int64_t)(hk * R + j) * D + tid]) : 0.f;
-      }
-      const int n_pairs = (2 + R) * D / 2;
-      for (int p = tid; p < n_pairs; p += NT) {
-        const int c = 2 * p;   // group-local channel; pairs never straddle q/k/v
-        int cg;
-        float* dst;
-        if (c < D) {
-          cg = hk * D + c;
-          dst = &sm.q[c];
-        } else if (c < 2 * D) {
-          cg = HK * D + hk * D + (c - D);
-          dst = &sm.k[c - D];
-        } else {
-          cg = 2 * HK * D + hk * R * D + (c - 2 * D);
-          dst = &sm.v[0][0] + (c - 2 * D);
+      for (int j = 0; j < kDecMaxR; ++j) zv[j] = cur.z[j];
+#pragma unroll
+      for (int pi = 0; pi < MAXP; ++pi) {
+        const int p = tid + pi * NT;
+        if (p < n_pairs) {
+          const int c = 2 * p;
+          int cg;
+          float* dst;
+          if (c < D) {
+            cg = hk * D + c;
+            dst = &sm.q[c];
+          } else if (c < 2 * D) {
+            cg = HK * D + hk * D + (c - D);
+            dst = &sm.k[c - D];
+          } else {
+            cg = 2 * HK * D + hk * R * D + (c - 2 * D);
+            dst = &sm.v[0][0] + (c - 2 * D);
+          }
+          union { uint32_t u; bf16 h[2]; } xu;
+          union { uint32_t u[T]; bf16 h[2 * T]; } tu, nu;
+          union { uint32_t u[K]; bf16 h[2 * K]; } wu;
+          xu.u = cur.x[pi];
+#pragma unroll
+          for (int i = 0; i < T; ++i) tu.u[i] = cur.taps[pi][i];
+#pragma unroll
+          for (int i = 0; i < K; ++i) wu.u[i] = cur.w[pi][i];
+#pragma unroll
+          for (int ch = 0; ch < 2; ++ch) {
+            float win[K], wv[K];
+#pragma unroll
+            for (int i = 0; i < T; ++i) win[i] = bf2f(tu.h[ch * T + i]);
+            win[T] = bf2f(xu.h[ch]);
+#pragma unroll
+            for (int i = 0; i < K; ++i) wv[i] = bf2f(wu.h[ch * K + i]);
+            dst[ch] = round_bf(conv_point<K>(win, wv));   // the conv output is bf16
+#pragma unroll
+            for (int i = 0; i + 1 < T; ++i) nu.h[ch * T + i] = tu.h[ch * T + i + 1];
+            nu.h[ch * T + T - 1] = xu.h[ch];
+          }
+          uint32_t* tp =
+              reinterpret_cast<uint32_t*>(conv_pool + slot * conv_ss + (int64_t)cg * T);
+#pragma unroll
+          for (int i = 0; i < T; ++i) tp[i] = nu.u[i];
         }
-        union { uint32_t u; bf16 h[2]; } xu;
-        union { uint32_t u[T]; bf16 h[2 * T]; } tu, nu;
-        union { uint32_t u[K]; bf16 h[2 * K]; } wu;
-        xu.u = *reinterpret_cast<const uint32_t*>(xrow + cg);
-        uint32_t* tp = reinterpret_cast<uint32_t*>(conv_pool + slot * conv_ss + (int64_t)cg * T);
-#pragma unroll
-        for (int i = 0; i < T; ++i) tu.u[i] = tp[i];
-#pragma unroll
-        for (int i = 0; i < K; ++i)
-          wu.u[i] = reinterpret_cast<const uint32_t*>(conv_w + (int64_t)cg * K)[i];
-#pragma unroll
-        for (int ch = 0; ch < 2; ++ch) {
-          float win[K], wv[K];
-#pragma unroll
-          for (int i = 0; i < T; ++i) win[i] = bf2f(tu.h[ch * T + i]);
-          win[T] = bf2f(xu.h[ch]);
-#pragma unroll
-          for (int i = 0; i < K; ++i) wv[i] = bf2f(wu.h[ch * K + i]);
-          dst[ch] = round_bf(conv_point<K>(win, wv));   // the conv output is bf16
-#pragma unroll
-          for (int i = 0; i + 1 < T; ++i) nu.h[ch * T + i] = tu.h[ch * T + i + 1];
-          nu.h[ch * T + T - 1] = xu.h[ch];
-        }
-#pragma unroll
-        for (int i = 0; i < T; ++i) tp[i] = nu.u[i];
       }
       if (tid < R) {
-        const int h = hk * R + tid;
-        const float al = param_f32 ? reinterpret_cast<const float*>(a_log)[h]
-                                   : bf2f(reinterpret_cast<const bf16*>(a_log)[h]);
-        const float db = param_f32 ? reinterpret_cast<const float*>(dt_bias)[h]
-                                   : bf2f(reinterpret_cast<const bf16*>(dt_bias)[h]);
         float gv, bt;
-        gate_value(bf2f(ap[(int64_t)b * abs_ + h]), bf2f(bp[(int64_t)b * abs_ + h]), al, db, gv,
-                   bt);
+        gate_value(cur.av, cur.bv, cur.al, cur.db, gv, bt);
         sm.gate_g[tid] = gv;
         sm.gate_b[tid] = bt;
       }
     }
+    if (gi + 1 < my_groups) fetch(gi + 1, cur);   // in flight during this group's units
     __syncthreads();
-    if (valid && tid < 32) {
+    // l2 norms of q and k: every warp computes them, identically (the same
+    // sums in the same order), so no second barrier is needed
+    if (valid) {
       float aq = 0.f, ak = 0.f;
-      for (int i = tid; i < D; i += 32) {
+      for (int i = lane; i < D; i += 32) {
         aq += sm.q[i] * sm.q[i];
         ak += sm.k[i] * sm.k[i];
       }
       aq = warp_sum(aq);
       ak = warp_sum(ak);
-      if (tid == 0) {
-        sm.norm[0] = rsqrtf(aq + 1e-6f);
-        sm.norm[1] = rsqrtf(ak + 1e-6f);
-      }
+      const float nq = rsqrtf(aq + 1e-6f) * scale;
+      const float nk = rsqrtf(ak + 1e-6f);
+      // this warp's rows: 32/CG row sets of RPT rows = 16 entries; lanes 0-15
+      // scale k, lanes 16-31 scale q
+      const int e = lane & 15;
+      const int rr = (tid >> 5) * (32 / CG) + e / RPT;
+      const int row = rr + RG * (e % RPT);
+      if (lane < 16) sm.kn[rr][e % RPT] = sm.k[row] * nk;
+      else sm.qn[rr][e % RPT] = sm.q[row] * nq;
+      __syncwarp();
     }
-    __syncthreads();
 
-    // ---- the R recurrence units of the group ----
+    // ---- the group's recurrence units: R heads x PARTS column parts ----
     for (int j = 0; j < R; ++j) {
-      const int u = gi * R + j;
-      const int stage = u % NSTAGE;
-      float4 s[RPT];
-      if (!tc::mbar_wait(tc::smem_u32(&sm.bar[stage]), (uint32_t)(u / NSTAGE) & 1u, kDecSpin)) {
-        sm.abort = 1;
-        if (status) atomicOr(status, GDN_STATUS_TIMEOUT);
-      }
-      consumed = u + 1;
-      if (valid) {
-        const float* st = sm.state[stage] + 4 * c4;
+      const int h = hk * R + j;
+      for (int part = 0; part < PARTS; ++part) {
+        const int u = gi * units_per_group + j * PARTS + part;
+        const int stage = u % NSTAGE;
+        Vec<VW> s[RPT];
+        if (!tc::mbar_wait(tc::smem_u32(&sm.bar[stage]), (uint32_t)(u / NSTAGE) & 1u,
+                           kDecSpin)) {
+          sm.abort = 1;
+          if (status) atomicOr(status, GDN_STATUS_TIMEOUT);
+        }
+        consumed = u + 1;
+        if (valid) {
+          const float* st = sm.state[stage] + VW * c4;
 #pragma unroll
-        for (int i = 0; i < RPT; ++i)
-          s[i] = *reinterpret_cast<const float4*>(st + (r0 + RG * i) * D);
+          for (int i = 0; i < RPT; ++i) {
+            if constexpr (VW == 2)
+              s[i].v = *reinterpret_cast<const float2*>(st + (r0 + RG * i) * kDecPartCols);
+            else
+              s[i].v = *reinterpret_cast<const float4*>(st + (r0 + RG * i) * kDecPartCols);
+          }
+        }
+        __syncthreads();   // stage consumed by every thread; abort flag visible
+        if (sm.abort) break;
+        if (tid == 0 && u + NSTAGE < n_units) issue(u + NSTAGE);
+        if (!valid) continue;
+        float px = 0.f;
+        if (pend) norm_sumsq(px);   // the previous head's norm, first half
+
+        const float eg = expf(sm.gate_g[j]);
+        const float bt = sm.gate_b[j];
+        const int col0 = part * kDecPartCols;
+
+        // S' = S * exp(g); partial (S'^T k^) over this thread's rows.
+        float kn[RPT];
+#pragma unroll
+        for (int i = 0; i < RPT; i += 4)
+          *reinterpret_cast<float4*>(&kn[i]) = *reinterpret_cast<const float4*>(&sm.kn[r0][i]);
+        Vec<VW> acc;
+#pragma unroll
+        for (int e = 0; e < VW; ++e) acc[e] = 0.f;
+#pragma unroll
+        for (int i = 0; i < RPT; ++i) {
+          const float kk = kn[i];
+#pragma unroll
+          for (int e = 0; e < VW; ++e) {
+            s[i][e] *= eg;
+            acc[e] += s[i][e] * kk;
+          }
+        }
+#pragma unroll
+        for (int e = 0; e < VW; ++e) sm.red[r0][VW * c4 + e] = acc[e];
+        __syncthreads();
+        if (pend) {                 // the previous head's norm, second half
+          norm_store(px, norm_inv());
+          pend = false;
+        }
+        if (tid < kDecPartCols) {
+          float kv = 0.f;
+#pragma unroll
+          for (int jj = 0; jj < RG; ++jj) kv += sm.red[jj][tid];
+          sm.delta[tid] = (sm.v[j][col0 + tid] - kv) * bt;
+        }
+        __syncthreads();
+
+        // S'' = S' + k^ (x) d, written back in place; partial (S''^T q^).
+        float* sbase = pool + slot * slot_stride + (int64_t)h * D * D + col0 + VW * c4;
+        float d[VW];
+#pragma unroll
+        for (int e = 0; e < VW; ++e) d[e] = sm.delta[VW * c4 + e];
+#pragma unroll
+        for (int e = 0; e < VW; ++e) acc[e] = 0.f;
+        float qn[RPT];
+#pragma unroll
+        for (int i = 0; i < RPT; i += 4)
+          *reinterpret_cast<float4*>(&qn[i]) = *reinterpret_cast<const float4*>(&sm.qn[r0][i]);
+#pragma unroll
+        for (int i = 0; i < RPT; ++i) {
+          const int r = r0 + RG * i;
+          const float kk = kn[i];
+          const float qq = qn[i];
+#pragma unroll
+          for (int e = 0; e < VW; ++e) s[i][e] += kk * d[e];
+          if constexpr (VW == 2)
+            __stcs(reinterpret_cast<float2*>(sbase + (int64_t)r * D), s[i].v);
+          else
+            __stcs(reinterpret_cast<float4*>(sbase + (int64_t)r * D), s[i].v);
+#pragma unroll
+          for (int e = 0; e < VW; ++e) acc[e] += s[i][e] * qq;
+        }
+#pragma unroll
+        for (int e = 0; e < VW; ++e) sm.red[r0][VW * c4 + e] = acc[e];
+        __syncthreads();
+        if (tid < kDecPartCols) {
+          float o = 0.f;
+#pragma unroll
+          for (int jj = 0; jj < RG; ++jj) o += sm.red[jj][tid];
+          sm.o[col0 + tid] = o;
+        }
       }
-      __syncthreads();   // stage consumed by every thread; abort flag visible
       if (sm.abort) break;
-      if (tid == 0 && u + NSTAGE < n_units) issue(u + NSTAGE);
       if (!valid) continue;
 
-      const int h = hk * R + j;
-      const float nq = sm.norm[0] * scale;
-      const float nk = sm.norm[1];
-      const float eg = expf(sm.gate_g[j]);
-      const float bt = sm.gate_b[j];
-
-      // S' = S * exp(g); partial (S'^T k^) over this thread's rows.
-      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+      // The head's gated RMSNorm: deferred into the next unit when that unit
+      // runs (it is valid), else done here on two barriers of its own.
+      pend = true;
+      prow = (int64_t)b * HV + h;
 #pragma unroll
-      for (int i = 0; i < RPT; ++i) {
-        const float kk = sm.k[r0 + RG * i] * nk;
-        s[i].x *= eg; s[i].y *= eg; s[i].z *= eg; s[i].w *= eg;
-        acc.x += s[i].x * kk; acc.y += s[i].y * kk; acc.z += s[i].z * kk; acc.w += s[i].w * kk;
-      }
-      *reinterpret_cast<float4*>(&sm.red[r0][4 * c4]) = acc;
-      __syncthreads();
-      if (tid < D) {
-        float kv = 0.f;
-#pragma unroll
-        for (int jj = 0; jj < RG; ++jj) kv += sm.red[jj][tid];
-        sm.delta[tid] = (sm.v[j][tid] - kv) * bt;
-      }
-      __syncthreads();
-
-      // S'' = S' + k^ (x) d, written back in place; partial (S''^T q^).
-      float* sbase = pool + slot * slot_stride + (int64_t)h * D * D + 4 * c4;
-      const float4 d = *reinterpret_cast<const float4*>(&sm.delta[4 * c4]);
-      acc = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
-      for (int i = 0; i < RPT; ++i) {
-        const int r = r0 + RG * i;
-        const float kk = sm.k[r] * nk;
-        const float qq = sm.q[r] * nq;
-        s[i].x += kk * d.x; s[i].y += kk * d.y; s[i].z += kk * d.z; s[i].w += kk * d.w;
-        __stcs(reinterpret_cast<float4*>(sbase + (int64_t)r * D), s[i]);
-        acc.x += s[i].x * qq; acc.y += s[i].y * qq; acc.z += s[i].z * qq; acc.w += s[i].w * qq;
-      }
-      *reinterpret_cast<float4*>(&sm.red[r0][4 * c4]) = acc;
-      __syncthreads();
-
-      // o = S''^T q^, then the gated RMSNorm of the row (bf16 core output first)
-      float x = 0.f;
-      if (tid < D) {
-        float o = 0.f;
-#pragma unroll
-        for (int jj = 0; jj < RG; ++jj) o += sm.red[jj][tid];
-        x = round_bf(o);
-      }
-      const float ss = warp_sum(x * x);
-      if ((tid & 31) == 0) sm.wsum[tid >> 5] = ss;
-      __syncthreads();
-      float tot = 0.f;
-#pragma unroll
-      for (int w = 0; w < NT / 32; ++w) tot += sm.wsum[w];
-      const float inv = rsqrtf(tot / (float)D + eps);
-      if (tid < D) {
-        float zz = 0.f;
-#pragma unroll
-        for (int jj = 0; jj < kDecMaxR; ++jj)
-          if (jj == j) zz = zv[jj];
-        out[((int64_t)b * HV + h) * D + tid] = f2bf(gated_norm_elem(x, inv, wn, zz));
+      for (int jj = 0; jj < kDecMaxR; ++jj)
+        if (jj == j) pz = zv[jj];
+      const bool next_runs =
+          j + 1 < R || (gi + 1 < my_groups && sm.slot[gi + 1] >= 0 &&
+                        sm.slot[gi + 1] < num_slots);
+      if (!next_runs) {
+        __syncthreads();
+        float x;
+        norm_sumsq(x);
+        __syncthreads();
+        norm_store(x, norm_inv());
+        pend = false;
       }
     }
     if (sm.abort) break;
@@ -317,14 +473,17 @@ __global__ void __launch_bounds__(DecCfg<D>::NT, DecCfg<D>::CTAS) decode_fused_k
 }
 
 template <int D, int K>
-static int launch_decode_fused(int grid, cudaStream_t s, const bf16* mixed, int64_t ms,
-                               const bf16* z, int64_t zs, const bf16* b, const bf16* a,
-                               int64_t abs_, bf16* conv_pool, int64_t conv_ss, const bf16* conv_w,
-                               const void* a_log, const void* dt_bias, int param_f32, float* pool,
+static int launch_decode_fused(int grid, cudaStream_t s, const CUtensorMap& tm,
+                               const bf16* mixed, int64_t ms, const bf16* z, int64_t zs,
+                               const bf16* b, const bf16* a, int64_t abs_, bf16* conv_pool,
+                               int64_t conv_ss, const bf16* conv_w, const void* a_log,
+                               const void* dt_bias, int param_f32, float* pool,
                                int64_t slot_stride, int64_t num_slots, const int64_t* ids,
                                const bf16* nw, float eps, bf16* out, int bs, int HK, int R,
                                float scale, int32_t* status) {
-  const size_t smem = sizeof(DecSmem<D>);
+  const size_t smem = sizeof(DecSmem<D>) + 128;   // + alignment slack
+  static_assert(DecCfg<D>::CTAS * (sizeof(DecSmem<D>) + 128 + 1024) <= 228 * 1024,
+                "the CTAs per SM must fit the shared memory");
   static int configured[64] = {0};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -339,9 +498,24 @@ static int launch_decode_fused(int grid, cudaStream_t s, const bf16* mixed, int6
     configured[dev] = 1;
   }
   decode_fused_kernel<D, K><<<grid, DecCfg<D>::NT, smem, s>>>(
-      mixed, ms, z, zs, b, a, abs_, conv_pool, conv_ss, conv_w, a_log, dt_bias, param_f32, pool,
-      slot_stride, num_slots, ids, nw, eps, out, bs, HK, R, scale, status);
+      tm, mixed, ms, z, zs, b, a, abs_, conv_pool, conv_ss, conv_w, a_log, dt_bias, param_f32,
+      pool, slot_stride, num_slots, ids, nw, eps, out, bs, HK, R, scale, status);
   return check_launch("gdn_decode_fused");
+}
+
+// fp32 [rows, D] view of a per-layer state pool: a (slot, head) tile starts at
+// row slot * slot_stride / D + head * D; boxes of [D rows x 64 columns].
+static bool make_state_map(CUtensorMap* m, const float* pool, int D, int64_t rows) {
+  EncodeTiledFn fn = encode_tiled();
+  if (fn == nullptr) return false;
+  const cuuint64_t dims[2] = {(cuuint64_t)D, (cuuint64_t)rows};
+  const cuuint64_t strides[1] = {(cuuint64_t)D * 4};
+  const cuuint32_t box[2] = {(cuuint32_t)kDecPartCols, (cuuint32_t)D};
+  const cuuint32_t estr[2] = {1, 1};
+  return fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(pool), dims, strides, box,
+            estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) ==
+         CUDA_SUCCESS;
 }
 
 }  // namespace gdn
@@ -379,6 +553,9 @@ extern "C" int gdn_decode_fused(const void* mixed, int64_t mixed_row_stride, con
   GDN_REQUIRE(num_slots > 0 && slot_stride >= value_dim * head_dim && slot_stride % 4 == 0,
               "gdn_decode_fused: slot_stride %lld must be >= HV*D*D and a multiple of 4",
               (long long)slot_stride);
+  GDN_UNSUPPORTED(slot_stride % head_dim == 0,
+                  "gdn_decode_fused: slot_stride %lld must be a multiple of the head dim",
+                  (long long)slot_stride);
   GDN_REQUIRE(conv_slot_stride >= conv_dim * (conv_kernel - 1),
               "gdn_decode_fused: conv_slot_stride %lld < conv_dim*(K-1)",
               (long long)conv_slot_stride);
@@ -393,6 +570,14 @@ extern "C" int gdn_decode_fused(const void* mixed, int64_t mixed_row_stride, con
                   "slots and conv weight 4-byte aligned");
   const int64_t groups = (int64_t)bs * num_k_heads;
   GDN_UNSUPPORTED(groups < (1ll << 30), "gdn_decode_fused: too many rows");
+  // the state pool as fp32 rows of head_dim: TMA row coordinates must fit int32
+  const int64_t rows = (num_slots - 1) * (slot_stride / head_dim) + value_dim;
+  GDN_UNSUPPORTED(rows < (1ll << 31), "gdn_decode_fused: state pool view too large for TMA");
+  CUtensorMap tm;
+  if (!make_state_map(&tm, s_pool, head_dim, rows)) {
+    set_error("gdn_decode_fused: cuTensorMapEncodeTiled failed");
+    return GDN_ERR_CUDA;
+  }
   const int ctas = head_dim == 128 ? DecCfg<128>::CTAS : DecCfg<64>::CTAS;
   int64_t grid = std::min<int64_t>(groups, (int64_t)sm_count() * ctas);
   const int64_t need = (groups + kDecMaxGroupsPerCta - 1) / kDecMaxGroupsPerCta;
@@ -402,7 +587,7 @@ extern "C" int gdn_decode_fused(const void* mixed, int64_t mixed_row_stride, con
 #define GDN_DF(DD, KK)                                                                          \
   if (head_dim == DD && conv_kernel == KK)                                                      \
     return launch_decode_fused<DD, KK>(                                                         \
-        (int)grid, s, (const bf16*)mixed, mixed_row_stride, (const bf16*)z, z_row_stride,       \
+        (int)grid, s, tm, (const bf16*)mixed, mixed_row_stride, (const bf16*)z, z_row_stride,       \
         (const bf16*)b, (const bf16*)a, ab_row_stride, (bf16*)conv_pool, conv_slot_stride,      \
         (const bf16*)conv_weight, a_log, dt_bias, pf, s_pool, slot_stride, num_slots, ids,      \
         (const bf16*)norm_weight, norm_eps, (bf16*)out, bs, num_k_heads, R, scale, status);

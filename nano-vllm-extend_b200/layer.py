@@ -55,11 +55,11 @@ class Qwen3_5GatedDeltaNet(nn.Module):
     installed); ``get_context`` returns the per-step Context.
     """
 
-    # Decode rows through the one-launch fused core (ops.decode_fused): None
-    # picks it where it is the faster route (ops.decode_fused_preferred),
-    # True whenever the shape allows, False never (the four operators; the
-    # results are identical).
-    fused_decode = None
+    # Decode rows through the one-launch fused core (ops.decode_fused) when the
+    # shape allows; it is the faster route at every batch size measured on
+    # B200 (bs 1..256).  False runs the four operators (identical results
+    # wherever their recurrent kernel runs full tiles).
+    fused_decode = True
 
     def __init__(self, config, parallel=None, get_context=None) -> None:
         super().__init__()
@@ -202,10 +202,7 @@ class Qwen3_5GatedDeltaNet(nn.Module):
         a_log = self.A_log[self._v_head_slice]
         dt_bias = self.dt_bias[self._v_head_slice]
         w = self.conv1d.weight.view(self.conv_dim, self.conv_kernel)
-        use = self.fused_decode
-        if use is None:
-            use = ops.decode_fused_preferred(mixed.shape[0], self.num_k_heads, mixed.device)
-        if use and ops.decode_fused_supported(self.num_k_heads, self.num_v_heads,
+        if self.fused_decode and ops.decode_fused_supported(self.num_k_heads, self.num_v_heads,
                                               self.head_k_dim, self.head_v_dim, self.conv_kernel):
             return ops.decode_fused(mixed, z, b, a, self.conv_cache, w, a_log, dt_bias,
                                     self.s_cache, ids, self.norm.weight, self.norm.eps)

@@ -335,23 +335,6 @@ def decode_fused_supported(num_k_heads: int, num_v_heads: int, head_k_dim: int,
             2 <= conv_kernel <= 4)
 
 
-_SM_COUNT: dict[int, int] = {}
-
-
-def decode_fused_preferred(bs: int, num_k_heads: int, device) -> bool:
-    """Whether the fused decode core beats the four-operator sequence for bs
-    rows: it does while the k-head groups (bs * num_k_heads, one CTA's work
-    item) number at most 4 per SM; above that the four-operator sequence's
-    register-resident recurrent kernel streams the state faster."""
-    device = torch.device(device)
-    idx = device.index if device.index is not None else torch.cuda.current_device()
-    n = _SM_COUNT.get(idx)
-    if n is None:
-        n = torch.cuda.get_device_properties(idx).multi_processor_count
-        _SM_COUNT[idx] = n
-    return bs * num_k_heads <= 4 * n
-
-
 def decode_fused(mixed: torch.Tensor, z: torch.Tensor, b: torch.Tensor, a: torch.Tensor,
                  conv_pool: torch.Tensor, conv_weight: torch.Tensor, a_log: torch.Tensor,
                  dt_bias: torch.Tensor, s_pool: torch.Tensor, ids: torch.Tensor,
