@@ -154,9 +154,10 @@ class Clocks:
 
 
 class DecodeStack:
-    def __init__(self, pkg, device, seed):
+    def __init__(self, pkg, device, seed, layers=None):
         self.pkg, self.dev = pkg, device
         c = C1
+        n_layers = c["layers"] if layers is None else layers
         cfg = type("Cfg", (), dict(hidden_size=c["hidden"], linear_num_key_heads=c["HK"],
                                    linear_num_value_heads=c["HV"], linear_key_head_dim=c["DK"],
                                    linear_value_head_dim=c["DV"], linear_conv_kernel_dim=c["K"],
@@ -166,7 +167,7 @@ class DecodeStack:
         torch.set_default_dtype(torch.bfloat16)
         try:
             with torch.device(device), torch.no_grad():
-                self.layers = [pkg.layer.Qwen3_5GatedDeltaNet(cfg) for _ in range(c["layers"])]
+                self.layers = [pkg.layer.Qwen3_5GatedDeltaNet(cfg) for _ in range(n_layers)]
                 for m in self.layers:
                     h = c["hidden"]
                     Fw = m._fused_weight()
@@ -195,6 +196,9 @@ class DecodeStack:
         return h
 
     def capture(self):
+        if not self.layers:          # an empty pipeline stage passes hidden through
+            self.y = self.x
+            return
         ctx = self.pkg.context
         ctx.set_context(self.cu, self.cu, 1, 1, linear_state_ids=self.ids)
         with torch.inference_mode():
@@ -207,7 +211,59 @@ class DecodeStack:
         ctx.reset_context()
 
     def replay(self):
-        self.graph.replay()
+        if self.graph is not None:
+            self.graph.replay()
+
+
+def pp_bench(pkg, dev, world, rank, steps, warmup):
+    """The config-1 decode stack as a `world`-stage pipeline: stage r runs its
+    contiguous layer range (split_layers) and hands (hidden, residual) to stage
+    r+1 through PipelineHandoff (one packed NCCL message on a side stream,
+    double-buffered, ordered by events) — the reference's two blocking
+    send/recv per boundary (engine/model_runner.py:795-810) replaced.  Stage r
+    starts step i+1 as soon as it has sent step i, so stages overlap across
+    steps.  Exposed handoff = (pipelined step time - slowest stage's compute
+    time) / pipelined step time, both CUDA-event timed, max over ranks."""
+    c = C1
+    P = pkg.parallel
+    lo, hi = P.split_layers(c["layers"], world, rank)
+    prev, nxt = P.pp_peers(rank, 1, world)
+    stack = DecodeStack(pkg, dev, seed=4321 + rank, layers=hi - lo)
+    stack.capture()
+    ho = P.PipelineHandoff(c["hidden"], c["bs"], torch.bfloat16, dev, prev, nxt, mode="packed")
+
+    def stage_only():
+        stack.replay()
+
+    def pp_step():
+        if prev is not None:
+            h, _ = ho.recv(c["bs"])
+            stack.x.copy_(h)
+        stack.replay()
+        if nxt is not None:
+            ho.send(stack.y, stack.x)
+
+    for _ in range(warmup):
+        stage_only()
+    t_stage = time_region(stage_only, steps, world)      # max over ranks
+    for _ in range(warmup):
+        pp_step()
+    ho.flush()
+    torch.cuda.synchronize()
+    t_pp = time_region(pp_step, steps, world)
+    ho.flush()
+    torch.cuda.synchronize()
+    barrier(world)
+    exposed = max(0.0, (t_pp - t_stage) / t_pp)
+    out = {"stages": world, "layers_per_stage": hi - lo,
+           "handoff": "PipelineHandoff packed (hidden, residual) over NCCL, side stream",
+           "bytes_per_handoff": 2 * c["bs"] * c["hidden"] * 2,
+           "ms_per_step_pipelined": round(t_pp / steps * 1e3, 4),
+           "ms_per_step_slowest_stage": round(t_stage / steps * 1e3, 4),
+           "exposed_handoff_frac": round(exposed, 4),
+           "tok_s_pipelined": round(c["bs"] * steps / t_pp, 1)}
+    stack.graph = None
+    return out
 
 
 def time_region(fn, steps, world, stream=None):
@@ -359,39 +415,59 @@ def prefill_bench(pkg, device, steps, peaks):
         torch.cuda.synchronize()
         per_step.append(e0.elapsed_time(e1) / 1e3)
     t = statistics.median(per_step)
-    # stage breakdown of one step and the chunk kernel alone (CUDA events)
+    # Stage breakdown of one step (CUDA events), the chunk kernel alone and the
+    # gated norm alone.  Every measured call runs once untimed first, so the
+    # caching allocator already holds its output blocks (a fresh multi-GB
+    # cudaMalloc next to the 40 GB decode stack costs ~100 ms).
     stages = {}
     with torch.inference_mode():
-        ev = [torch.cuda.Event(enable_timing=True) for _ in range(8)]
-        pools.reset(ids)
-        ev[0].record()
-        proj = torch.nn.functional.linear(x, m._fused_weight())
-        ev[1].record()
-        r = m._proj_rows
-        gg, beta = pkg.ops.fused_g_beta(proj[:, r[1]:r[2]], proj[:, r[2]:r[3]],
-                                        m.A_log, m.dt_bias)
-        ev[2].record()
-        y = pkg.ops.causal_conv_silu_varlen(proj[:, :m.conv_dim], m.conv_cache, ids,
-                                            m.conv1d.weight, cu)
-        ev[3].record()
-        q, k, v = m._split(y)
-        z = proj[:, r[0]:r[1]].view(N, c["HV"], c["DV"])
-        core = pkg.ops.chunk_gated_delta_rule_varlen(q, k, v, gg, beta, m.s_cache, ids, cu,
-                                                     max(lens), z=z, norm_weight=m.norm.weight)
-        ev[4].record()
-        m.out_proj(core.view(N, c["HV"] * c["DV"]))
-        ev[5].record()
+        for rep in range(2):
+            ev = [torch.cuda.Event(enable_timing=True) for _ in range(8)]
+            pools.reset(ids)
+            ev[0].record()
+            proj = torch.nn.functional.linear(x, m._fused_weight())
+            ev[1].record()
+            r = m._proj_rows
+            gg, beta = pkg.ops.fused_g_beta(proj[:, r[1]:r[2]], proj[:, r[2]:r[3]],
+                                            m.A_log, m.dt_bias)
+            ev[2].record()
+            y = pkg.ops.causal_conv_silu_varlen(proj[:, :m.conv_dim], m.conv_cache, ids,
+                                                m.conv1d.weight, cu)
+            ev[3].record()
+            q, k, v = m._split(y)
+            z = proj[:, r[0]:r[1]].view(N, c["HV"], c["DV"])
+            core = pkg.ops.chunk_gated_delta_rule_varlen(q, k, v, gg, beta, m.s_cache, ids, cu,
+                                                         max(lens), z=z,
+                                                         norm_weight=m.norm.weight)
+            ev[4].record()
+            m.out_proj(core.view(N, c["HV"] * c["DV"]))
+            ev[5].record()
+            torch.cuda.synchronize()
+            for i, name in enumerate(["in_proj_gemm", "gate", "conv", "chunk_with_norm",
+                                      "out_proj_gemm"]):
+                stages[name] = round(ev[i].elapsed_time(ev[i + 1]), 3)
+            del core
+        pkg.ops.chunk_gated_delta_rule_varlen(q, k, v, gg, beta, m.s_cache, ids, cu, max(lens))
         torch.cuda.synchronize()
-        for i, name in enumerate(["in_proj_gemm", "gate", "conv", "chunk_with_norm",
-                                  "out_proj_gemm"]):
-            stages[name] = round(ev[i].elapsed_time(ev[i + 1]), 3)
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record()
         for _ in range(steps):
             pkg.ops.chunk_gated_delta_rule_varlen(q, k, v, gg, beta, m.s_cache, ids, cu,
-                                                  max(lens), z=z, norm_weight=m.norm.weight)
+                                                  max(lens))
         e1.record()
         torch.cuda.synchronize()
+        o = pkg.ops.chunk_gated_delta_rule_varlen(q, k, v, gg, beta, m.s_cache, ids, cu,
+                                                  max(lens))
+        pkg.ops.rms_norm_gated(o, z, m.norm.weight, 1e-6)
+        torch.cuda.synchronize()
+        n0, n1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        n0.record()
+        for _ in range(steps):
+            pkg.ops.rms_norm_gated(o, z, m.norm.weight, 1e-6)
+        n1.record()
+        torch.cuda.synchronize()
+    tn = n0.elapsed_time(n1) / 1e3 / steps
+    norm_bytes = 3 * N * c["HV"] * c["DV"] * 2
     tk = e0.elapsed_time(e1) / 1e3 / steps
     flops = CHUNK_FLOPS_PER_TOKEN_HEAD * N * c["HV"]
     achieved = flops / tk / 1e12
@@ -399,7 +475,11 @@ def prefill_bench(pkg, device, steps, peaks):
                         f"{N} tokens, full layer forward",
             "value": round(N / t, 1), "unit": "tok/s", "tokens": N, "ms_per_step": round(t * 1e3, 3),
             "ms_per_step_min": round(min(per_step) * 1e3, 3), "stages_ms": stages,
-            "chunk_kernel": {"kernel": "chunk_prefill_tc_kernel (gated norm fused)",
+            "norm_kernel": {"kernel": "rms_gated_kernel (config-2 core output)",
+                            "ms": round(tn * 1e3, 3), "bound": "hbm",
+                            "achieved": round(norm_bytes / tn / 1e9, 1), "unit": "GB/s",
+                            "frac": round(norm_bytes / tn / 1e9 / peaks["hbm_gbs"], 4)},
+            "chunk_kernel": {"kernel": "chunk_prefill_tc_kernel",
                              "bound": "tensor",
                              "ms": round(tk * 1e3, 3), "tok_s": round(N / tk, 1),
                              "achieved": round(achieved, 2), "unit": "TFLOP/s",
@@ -647,6 +727,8 @@ def main():
             "gpu_launches": (1 if stack.layers[0].fused_decode else 3) * c["layers"] * args.steps,
             "clocks": clk}
 
+    if world > 1:
+        line["pp"] = pp_bench(pkg, dev, world, rank, min(args.steps, 200), args.warmup)
     if rank == 0 and world == 1 and not args.no_prefill:
         try:
             line["prefill"] = prefill_bench(pkg, dev, args.prefill_steps, peaks)

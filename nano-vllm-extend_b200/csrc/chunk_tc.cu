@@ -46,6 +46,7 @@ namespace tc {
 
 constexpr int kC = 64;
 constexpr int kD = 128;
+constexpr int kLptMaxSeqs = 256;   // longest-first chain order up to this many sequences
 constexpr int kThreads = 128;
 constexpr uint32_t kSpin = 1u << 22;
 constexpr uint32_t kTmemCols = 256;
@@ -167,6 +168,32 @@ __device__ __forceinline__ void invert_unit_lower(float (*LT)[kLP], float* X, in
   __syncthreads();
 }
 
+// Longest chains first: CTA rank k (of n_seqs) takes the sequence with the
+// k-th largest length (ties by index), so the long serial chains start in the
+// first wave and the short ones fill in behind them.  The ranks form a
+// permutation for any cu_seqlens, malformed ones included.  Kept out of line so
+// it does not weigh on the main loop's register allocation.
+__device__ __noinline__ int lpt_sequence(const int32_t* __restrict__ cu, int n_seqs, int rank,
+                                         int tid) {
+  __shared__ int s_len[kLptMaxSeqs];
+  __shared__ int s_seq;
+  if (n_seqs > kLptMaxSeqs) return rank;
+  for (int i = tid; i < n_seqs; i += kThreads) s_len[i] = cu[i + 1] - cu[i];
+  if (tid == 0) s_seq = rank;
+  __syncthreads();
+  for (int i = tid; i < n_seqs; i += kThreads) {
+    const int li = s_len[i];
+    int rk = 0;
+    for (int j = 0; j < n_seqs; ++j) {
+      const int lj = s_len[j];
+      rk += (lj > li) || (lj == li && j < i);
+    }
+    if (rk == rank) s_seq = i;
+  }
+  __syncthreads();
+  return s_seq;
+}
+
 __global__ void __launch_bounds__(kThreads, 2) chunk_prefill_tc_kernel(
     const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
     const __grid_constant__ CUtensorMap tm_v, const float* __restrict__ g,
@@ -179,9 +206,10 @@ __global__ void __launch_bounds__(kThreads, 2) chunk_prefill_tc_kernel(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int tid = threadIdx.x;
   const int warp = tid >> 5, lane = tid & 31;
-  const int r = blockIdx.x / HV;
-  const int h = blockIdx.x - r * HV;
+  const int rank = blockIdx.x / HV;
+  const int h = blockIdx.x - rank * HV;
   const int hk = h / (HV / HK);
+  const int r = lpt_sequence(cu, gridDim.x / HV, rank, tid);
 
   const int64_t slot = ids[r];
   if (!slot_ok(slot, num_slots, status)) return;

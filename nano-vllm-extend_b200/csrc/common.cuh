@@ -27,7 +27,9 @@ int launch_rms_norm_gated(const void* x, const void* gate, int64_t gate_token_st
                           int dim, float eps, cudaStream_t s);
 
 // The reference's gated-norm rounding for one element (qwen3_5.py:127-131):
-// y = bf16(bf16(w * bf16(x * inv)) * silu(z)), fp32 arithmetic.
+// y = bf16(bf16(w * bf16(x * inv)) * silu(z)), fp32 arithmetic; silu with the
+// hardware exp2 / reciprocal approximations (a few fp32 ulps before the final
+// bf16 rounding), which keeps the prefill norm HBM-bound.
 __device__ __forceinline__ float gated_norm_elem(float x, float inv, float w, float z);
 
 #define GDN_REQUIRE(cond, ...)                       \
@@ -58,7 +60,7 @@ __device__ __forceinline__ float siluf_(float x) { return x * sigmoidf_(x); }
 __device__ __forceinline__ float gated_norm_elem(float x, float inv, float w, float z) {
   const float t = __bfloat162float(__float2bfloat16_rn(x * inv));
   const float u = __bfloat162float(__float2bfloat16_rn(w * t));
-  return u * siluf_(z);
+  return u * __fdividef(z, 1.0f + __expf(-z));
 }
 
 // Depthwise conv tap sum + SiLU for one channel: acc = sum_{i<K} w[i] *

@@ -39,42 +39,57 @@ __global__ void __launch_bounds__(256) gbeta_kernel(
 // Gated RMSNorm, y = bf16(bf16(w * bf16(x * rsqrt(mean x^2 + eps))) * silu(gate)), the
 // rounding sequence of qwen3_5.py:121-131 for a bf16 model.  Each lane moves 8
 // elements as 16-byte vectors; DIM/8 lanes share a row and reduce by shuffles.
+// A warp issues the loads of U row sets (U * 32 / (DIM/8) rows) before it
+// computes any of them, so each lane keeps U x 32 bytes in flight.
 // x and y may alias: a row's lanes read it fully before any of them writes.
 template <int DIM>
-__global__ void __launch_bounds__(256) rms_gated_kernel(
+__global__ void __launch_bounds__(256, 3) rms_gated_kernel(
     const bf16* x, const bf16* __restrict__ gate, int64_t gate_token_stride,
     int heads, const bf16* __restrict__ w, bf16* y, int64_t n_rows, float eps) {
   constexpr int LPR = DIM / 8;                 // lanes per row
-  constexpr int RPW = 32 / LPR;                // rows per warp
+  constexpr int RPW = 32 / LPR;                // rows per warp and row set
+  constexpr int U = 4;                         // row sets in flight per warp
   const int lane = threadIdx.x & 31;
   const int sub = lane % LPR;
   float wv[8];
   unpack8(*reinterpret_cast<const uint4*>(w + sub * 8), wv);
-  const int64_t rows_per_iter = (int64_t)gridDim.x * (blockDim.x >> 5) * RPW;
+  const int64_t rows_per_iter = (int64_t)gridDim.x * (blockDim.x >> 5) * RPW * U;
   // warp-uniform loop bound: every lane of a warp runs the same iterations
-  for (int64_t base = ((int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5)) * RPW;
+  for (int64_t base = ((int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5)) * RPW * U;
        base < n_rows; base += rows_per_iter) {
-    const int64_t row = base + lane / LPR;
-    const bool active = row < n_rows;
-    float xv[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f}, gv[8];
-    if (active) {
-      unpack8(*reinterpret_cast<const uint4*>(x + row * DIM + sub * 8), xv);
-      const int64_t tok = row / heads;
-      unpack8(*reinterpret_cast<const uint4*>(gate + tok * gate_token_stride +
-                                              (row - tok * heads) * DIM + sub * 8),
-              gv);
+    const int64_t row0 = base + lane / LPR;
+    uint4 xr[U], gr[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int64_t row = row0 + u * RPW;
+      xr[u] = make_uint4(0u, 0u, 0u, 0u);
+      gr[u] = make_uint4(0u, 0u, 0u, 0u);
+      if (row < n_rows) {
+        xr[u] = *reinterpret_cast<const uint4*>(x + row * DIM + sub * 8);
+        const uint32_t tok = (uint32_t)row / (uint32_t)heads;   // n_rows < 2^32 (host check)
+        const uint32_t hh = (uint32_t)row - tok * (uint32_t)heads;
+        gr[u] = *reinterpret_cast<const uint4*>(gate + (int64_t)tok * gate_token_stride +
+                                                hh * DIM + sub * 8);
+      }
     }
-    float ss = 0.f;
 #pragma unroll
-    for (int e = 0; e < 8; ++e) ss += xv[e] * xv[e];
+    for (int u = 0; u < U; ++u) {
+      const int64_t row = row0 + u * RPW;
+      float xv[8], gv[8];
+      unpack8(xr[u], xv);
+      unpack8(gr[u], gv);
+      float ss = 0.f;
 #pragma unroll
-    for (int o = LPR / 2; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-    const float inv = rsqrtf(ss / (float)DIM + eps);
-    if (active) {
-      float yv[8];
+      for (int e = 0; e < 8; ++e) ss += xv[e] * xv[e];
 #pragma unroll
-      for (int e = 0; e < 8; ++e) yv[e] = gated_norm_elem(xv[e], inv, wv[e], gv[e]);
-      *reinterpret_cast<uint4*>(y + row * DIM + sub * 8) = pack8(yv);
+      for (int o = LPR / 2; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+      const float inv = rsqrtf(ss / (float)DIM + eps);
+      if (row < n_rows) {
+        float yv[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) yv[e] = gated_norm_elem(xv[e], inv, wv[e], gv[e]);
+        *reinterpret_cast<uint4*>(y + row * DIM + sub * 8) = pack8(yv);
+      }
     }
   }
 }
@@ -83,10 +98,12 @@ int launch_rms_norm_gated(const void* x, const void* gate, int64_t gate_token_st
                           int heads_per_token, const void* weight, void* y, int64_t n_rows,
                           int dim, float eps, cudaStream_t s) {
   if (n_rows == 0) return GDN_OK;
+  GDN_UNSUPPORTED(n_rows < (1ll << 32), "gated norm: %lld rows (max 2^32 - 1)", (long long)n_rows);
   GDN_UNSUPPORTED(((uintptr_t)x | (uintptr_t)gate | (uintptr_t)weight | (uintptr_t)y) % 16 == 0 &&
                       gate_token_stride % 8 == 0,
                   "gated norm: operands must be 16-byte aligned");
-  int64_t blocks = (n_rows + 31) / 32;
+  const int64_t rows_per_block = 8 * (32 / (dim / 8)) * 4;   // warps x rows x row sets
+  int64_t blocks = (n_rows + rows_per_block - 1) / rows_per_block;
   const int64_t cap = (int64_t)sm_count() * 8;
   if (blocks > cap) blocks = cap;
 #define GDN_NORM_CASE(D)                                                                        \
