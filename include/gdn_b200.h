@@ -38,7 +38,7 @@
 extern "C" {
 #endif
 
-#define GDN_ABI_VERSION 3
+#define GDN_ABI_VERSION 4
 
 enum gdn_status_code {
   GDN_OK = 0,
@@ -210,6 +210,13 @@ int gdn_rms_norm_gated(const void* x, const void* gate, int64_t gate_token_strid
  * 2..4; s_pool 16-byte aligned; mixed rows, conv slots and conv weight 4-byte
  * aligned (even strides).  A row whose slot id is out of range is skipped
  * (GDN_STATUS_BAD_SLOT), its out rows are left unwritten.
+ * group_counters: int32 scratch of at least bs * num_k_heads entries, all zero
+ * on entry and left all zero on return (the v-heads of a k-head count their
+ * reads of the shared q/k conv state there; the last one rolls it).  With it,
+ * batches whose bs * num_v_heads units fit one wave of the GPU run one CTA per
+ * (row, v-head) with the state staged in shared memory (the low-latency form);
+ * larger batches, and every batch when it is NULL, run a persistent form that
+ * needs no scratch.  Calls that share a counter array must not overlap in time.
  */
 int gdn_decode_fused(const void* mixed, int64_t mixed_row_stride,
                      const void* z, int64_t z_row_stride,
@@ -220,7 +227,8 @@ int gdn_decode_fused(const void* mixed, int64_t mixed_row_stride,
                      float* s_pool, int64_t slot_stride, int64_t num_slots,
                      const int64_t* ids, const void* norm_weight, float norm_eps,
                      void* out, int32_t bs, int32_t num_k_heads, int32_t num_v_heads,
-                     int32_t head_dim, float scale, int32_t* status, void* stream);
+                     int32_t head_dim, float scale, int32_t* group_counters,
+                     int32_t* status, void* stream);
 
 #ifdef __cplusplus
 }

@@ -335,10 +335,30 @@ def decode_fused_supported(num_k_heads: int, num_v_heads: int, head_k_dim: int,
             2 <= conv_kernel <= 4)
 
 
+_COUNTERS: dict[int, torch.Tensor] = {}
+
+
+def group_counters(device, n: int) -> torch.Tensor:
+    """The per-device int32 scratch of decode_fused's group counters (at least
+    n entries; all zero between calls — the kernel leaves them zero).  Made
+    outside inference mode so it is a normal tensor; when it has to grow it
+    is replaced, so call this once with the largest batch before capturing
+    a CUDA graph (the layer does so on its eager warm-up steps)."""
+    device = torch.device(device)
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    t = _COUNTERS.get(idx)
+    if t is None or t.numel() < n:
+        with torch.inference_mode(False):
+            t = torch.zeros(max(n, 4096), dtype=torch.int32, device=torch.device("cuda", idx))
+        _COUNTERS[idx] = t
+    return t
+
+
 def decode_fused(mixed: torch.Tensor, z: torch.Tensor, b: torch.Tensor, a: torch.Tensor,
                  conv_pool: torch.Tensor, conv_weight: torch.Tensor, a_log: torch.Tensor,
                  dt_bias: torch.Tensor, s_pool: torch.Tensor, ids: torch.Tensor,
-                 norm_weight: torch.Tensor, eps: float = 1e-6) -> torch.Tensor:
+                 norm_weight: torch.Tensor, eps: float = 1e-6,
+                 counters: bool = True) -> torch.Tensor:
     """The decode branch of Qwen3_5GatedDeltaNet.forward for T == 1 rows in one
     kernel: conv_decode_step (qwen3_5.py:1008-1012) + fused_g_beta (:976-982)
     + recurrent_gdn_inplace (:1013-1026) + the gated norm (:1083-1085).
@@ -347,7 +367,10 @@ def decode_fused(mixed: torch.Tensor, z: torch.Tensor, b: torch.Tensor, a: torch
     (shared row stride); conv_pool [slots, conv_dim, K-1] and s_pool [slots,
     HV, D, D] per-layer views rolled / updated in place at rows ``ids``.
     Returns the normed core output [bs, HV, D] (bit-identical to the
-    four-operator sequence)."""
+    four-operator sequence).  ``counters`` passes this device's group-counter
+    scratch (:func:`group_counters`), which lets batches that fit one wave of
+    the GPU run the low-latency head-per-CTA kernel; False always runs the
+    persistent kernel, which needs no scratch."""
     _cuda(mixed, z, b, a, conv_pool, conv_weight, a_log, dt_bias, s_pool, ids, norm_weight)
     bs = mixed.shape[0]
     HV, DK, DV = s_pool.shape[1], s_pool.shape[2], s_pool.shape[3]
@@ -374,10 +397,11 @@ def decode_fused(mixed: torch.Tensor, z: torch.Tensor, b: torch.Tensor, a: torch
     assert ids.numel() == bs
     assert conv_pool.shape[0] == s_pool.shape[0], "both pools index the same slots"
     out = torch.empty(bs, HV, D, dtype=torch.bfloat16, device=mixed.device)
+    cnt = group_counters(mixed.device, bs * HK) if counters else None
     rc = _lib.load().gdn_decode_fused(
         _p(m2), ms, _p(z3), zs, _p(b), _p(a), b.stride(0), _p(conv_pool), _slot_stride(conv_pool),
         _p(w), K, _p(a_log.contiguous()), _p(dt_bias.contiguous()), pdt, _p(s_pool),
         _slot_stride(s_pool), s_pool.shape[0], _p(ids), _p(nw), float(eps), _p(out), bs, HK, HV,
-        D, D ** -0.5, _p(status_word(mixed.device)), _stream_ptr(mixed.device))
+        D, D ** -0.5, _p(cnt), _p(status_word(mixed.device)), _stream_ptr(mixed.device))
     _lib.check(rc, "gdn_decode_fused")
     return out

@@ -112,7 +112,7 @@ def _decode_fused_args(**kw):
     a = dict(mixed=None, ms=8192, z=None, zs=4096, b=None, a=None, abs_=8, conv_pool=None,
              conv_ss=8192 * 3, conv_w=None, K=4, a_log=None, dt_bias=None, pdt=0, s_pool=None,
              slot_stride=4 * 128 * 128, num_slots=2, ids=None, nw=None, eps=1e-6, out=None, bs=1,
-             HK=2, HV=4, D=128, scale=0.1, status=None, stream=None)
+             HK=2, HV=4, D=128, scale=0.1, counters=None, status=None, stream=None)
     a.update(kw)
     return list(a.values())
 

@@ -69,7 +69,7 @@ def views(c, proj_d):
     return mixed, z, b, a
 
 
-def run_fused(ops, c, pdt):
+def run_fused(ops, c, pdt, counters=True):
     proj_d = dev(c["proj"], torch.bfloat16)
     mixed, z, b, a = views(c, proj_d)
     s_d = dev(c["s_pool"])
@@ -78,7 +78,7 @@ def run_fused(ops, c, pdt):
     out = ops.decode_fused(mixed, z, b, a, cv_d[:, L], dev(c["conv_w"], torch.bfloat16),
                            dev(c["a_log"], pdt), dev(c["dt_bias"], pdt), s_d[:, L],
                            torch.as_tensor(c["ids"], device=DEV), dev(c["norm_w"], torch.bfloat16),
-                           1e-6)
+                           1e-6, counters=counters)
     return out, s_d, cv_d
 
 
@@ -111,11 +111,18 @@ CASES = [
 ]
 
 
+def counters_zero(ops):
+    t = ops._COUNTERS.get(0)
+    return t is None or int(t.abs().sum().item()) == 0
+
+
+@pytest.mark.parametrize("counters", [True, False])   # head-per-CTA / persistent form
 @pytest.mark.parametrize("HK,HV,D,K,bs,pdt", CASES)
-def test_decode_fused_vs_oracle(ops, HK, HV, D, K, bs, pdt):
+def test_decode_fused_vs_oracle(ops, HK, HV, D, K, bs, pdt, counters):
     c = make_case(HK, HV, D, K, bs, seed=500 + bs + D)
-    out, s_d, cv_d = run_fused(ops, c, pdt)
+    out, s_d, cv_d = run_fused(ops, c, pdt, counters)
     ops.check_status()
+    assert counters_zero(ops)
     L, ids = c["layer"], c["ids"]
     C = c["C"]
     p = c["proj"]
@@ -136,10 +143,11 @@ def test_decode_fused_vs_oracle(ops, HK, HV, D, K, bs, pdt):
     assert np.array_equal(s_got[:, 0], c["s_pool"][:, 0])
 
 
+@pytest.mark.parametrize("counters", [True, False])
 @pytest.mark.parametrize("HK,HV,D,K,bs,pdt", CASES)
-def test_decode_fused_equals_four_operators(ops, HK, HV, D, K, bs, pdt):
+def test_decode_fused_equals_four_operators(ops, HK, HV, D, K, bs, pdt, counters):
     c = make_case(HK, HV, D, K, bs, seed=700 + bs + D)
-    f_out, f_s, f_cv = run_fused(ops, c, pdt)
+    f_out, f_s, f_cv = run_fused(ops, c, pdt, counters)
     u_out, u_s, u_cv = run_four_ops(ops, c, pdt)
     torch.cuda.synchronize()
     assert torch.equal(f_cv, u_cv)
@@ -184,15 +192,17 @@ def test_decode_fused_two_steps_in_a_row(ops):
     assert state_rel(host(s_d)[c1["ids"], L], s_ref[c1["ids"], L]) <= STATE_RTOL
 
 
-def test_decode_fused_bad_slot_is_flagged_not_touched(ops):
+@pytest.mark.parametrize("counters", [True, False])
+def test_decode_fused_bad_slot_is_flagged_not_touched(ops, counters):
     HK, HV, D, K, bs = 2, 4, 128, 4, 4
     c = make_case(HK, HV, D, K, bs, seed=950, slots_extra=0)
     slots = c["s_pool"].shape[0]
     c["ids"] = np.array([1, slots, -1, 2])             # rows 1 and 2 out of range
     ops.check_status()
-    out, s_d, cv_d = run_fused(ops, c, torch.float32)
+    out, s_d, cv_d = run_fused(ops, c, torch.float32, counters)
     with pytest.raises(IndexError):
         ops.check_status()
+    assert counters_zero(ops)
     s_got, cv_got = host(s_d), host(cv_d)
     keep = [0, 3]                                      # slots no valid row names
     assert np.array_equal(s_got[keep], c["s_pool"][keep])
