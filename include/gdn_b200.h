@@ -230,6 +230,31 @@ int gdn_decode_fused(const void* mixed, int64_t mixed_row_stride,
                      int32_t head_dim, float scale, int32_t* group_counters,
                      int32_t* status, void* stream);
 
+/*
+ * gdn_decode_fused without caller scratch (no counterpart in the reference):
+ * the same arguments minus group_counters, the same results.  The group
+ * counters live in a static device array of this library, sized for
+ * bs * num_k_heads <= 16384; larger batches are rejected with
+ * GDN_ERR_UNSUPPORTED.  For callers that hold no device allocator at the call
+ * site (a host binding the C ABI that receives the engine's buffers as raw
+ * device pointers) or that must not allocate per decode step.  The array is
+ * zero when the library loads and each call leaves it zero, so it needs no
+ * clearing.  The first call on a device looks its address up (with that device
+ * current); make that first call before any stream capture.  Calls on one
+ * device share the array: they must not overlap in time (different streams
+ * running it concurrently race on the counters).
+ */
+int gdn_decode_fused_static(const void* mixed, int64_t mixed_row_stride,
+                            const void* z, int64_t z_row_stride,
+                            const void* b, const void* a, int64_t ab_row_stride,
+                            void* conv_pool, int64_t conv_slot_stride,
+                            const void* conv_weight, int32_t conv_kernel,
+                            const void* a_log, const void* dt_bias, int32_t param_dtype,
+                            float* s_pool, int64_t slot_stride, int64_t num_slots,
+                            const int64_t* ids, const void* norm_weight, float norm_eps,
+                            void* out, int32_t bs, int32_t num_k_heads, int32_t num_v_heads,
+                            int32_t head_dim, float scale, int32_t* status, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -40,6 +40,8 @@ SIGNATURES = {
     "gdn_rms_norm_gated": [vp, vp, i64, i32, vp, vp, i64, i32, f32, vp],
     "gdn_decode_fused": [vp, i64, vp, i64, vp, vp, i64, vp, i64, vp, i32, vp, vp, i32, vp, i64,
                          i64, vp, vp, f32, vp, i32, i32, i32, i32, f32, vp, vp, vp],
+    "gdn_decode_fused_static": [vp, i64, vp, i64, vp, vp, i64, vp, i64, vp, i32, vp, vp, i32, vp,
+                                i64, i64, vp, vp, f32, vp, i32, i32, i32, i32, f32, vp, vp],
 }
 
 _LIB = None

@@ -876,3 +876,67 @@ extern "C" int gdn_decode_fused(const void* mixed, int64_t mixed_row_stride, con
   set_error("gdn_decode_fused: unsupported configuration");
   return GDN_ERR_UNSUPPORTED;
 }
+
+// ---------------------------------------------------------------------------
+// gdn_decode_fused without caller scratch: the group counters live in a
+// file-scope device array.  It is zero when the module loads and every launch
+// leaves it zero (the last reader of a group resets its counter), so nothing
+// has to clear it.  Its address is looked up once per device, on the first call
+// made with that device current.
+// ---------------------------------------------------------------------------
+namespace gdn {
+
+constexpr int64_t kStaticMaxGroups = 16384;   // bs * num_k_heads, 64 KiB of counters
+static __device__ __align__(256) int32_t g_static_group_counters[kStaticMaxGroups];
+
+static int32_t* static_group_counters() {
+  static int32_t* ptr[64] = {nullptr};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
+    set_error("gdn_decode_fused_static: no current CUDA device (or device index >= 64)");
+    return nullptr;
+  }
+  if (ptr[dev] == nullptr) {
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_static_group_counters);
+    if (e != cudaSuccess || p == nullptr) {
+      set_error("gdn_decode_fused_static: cudaGetSymbolAddress failed: %s",
+                cudaGetErrorString(e));
+      return nullptr;
+    }
+    ptr[dev] = static_cast<int32_t*>(p);
+  }
+  return ptr[dev];
+}
+
+}  // namespace gdn
+
+extern "C" int gdn_decode_fused_static(
+    const void* mixed, int64_t mixed_row_stride, const void* z, int64_t z_row_stride,
+    const void* b, const void* a, int64_t ab_row_stride, void* conv_pool, int64_t conv_slot_stride,
+    const void* conv_weight, int32_t conv_kernel, const void* a_log, const void* dt_bias,
+    int32_t param_dtype, float* s_pool, int64_t slot_stride, int64_t num_slots, const int64_t* ids,
+    const void* norm_weight, float norm_eps, void* out, int32_t bs, int32_t num_k_heads,
+    int32_t num_v_heads, int32_t head_dim, float scale, int32_t* status, void* stream) {
+  clear_error();
+  GDN_REQUIRE(bs >= 0 && num_k_heads > 0, "gdn_decode_fused_static: bad sizes (bs=%d, HK=%d)",
+              bs, num_k_heads);
+  const int64_t groups = (int64_t)bs * num_k_heads;
+  GDN_UNSUPPORTED(groups <= kStaticMaxGroups,
+                  "gdn_decode_fused_static: bs * num_k_heads = %lld exceeds its static scratch "
+                  "of %lld groups (use gdn_decode_fused with caller scratch)",
+                  (long long)groups, (long long)kStaticMaxGroups);
+  if (bs == 0)
+    return gdn_decode_fused(mixed, mixed_row_stride, z, z_row_stride, b, a, ab_row_stride,
+                            conv_pool, conv_slot_stride, conv_weight, conv_kernel, a_log, dt_bias,
+                            param_dtype, s_pool, slot_stride, num_slots, ids, norm_weight,
+                            norm_eps, out, bs, num_k_heads, num_v_heads, head_dim, scale, nullptr,
+                            status, stream);
+  int32_t* counters = static_group_counters();
+  if (counters == nullptr) return GDN_ERR_CUDA;
+  return gdn_decode_fused(mixed, mixed_row_stride, z, z_row_stride, b, a, ab_row_stride,
+                          conv_pool, conv_slot_stride, conv_weight, conv_kernel, a_log, dt_bias,
+                          param_dtype, s_pool, slot_stride, num_slots, ids, norm_weight, norm_eps,
+                          out, bs, num_k_heads, num_v_heads, head_dim, scale, counters, status,
+                          stream);
+}
