@@ -336,20 +336,24 @@ def decode_fused_supported(num_k_heads: int, num_v_heads: int, head_k_dim: int,
 
 
 _COUNTERS: dict[int, torch.Tensor] = {}
+_RETIRED_COUNTERS: list[torch.Tensor] = []
 
 
 def group_counters(device, n: int) -> torch.Tensor:
     """The per-device int32 scratch of decode_fused's group counters (at least
     n entries; all zero between calls — the kernel leaves them zero).  Made
-    outside inference mode so it is a normal tensor; when it has to grow it
-    is replaced, so call this once with the largest batch before capturing
-    a CUDA graph (the layer does so on its eager warm-up steps)."""
+    outside inference mode so it is a normal tensor, 65536 entries (256 KiB)
+    at first so it practically never grows; a buffer that is outgrown stays
+    allocated, because CUDA graphs captured earlier keep its address."""
     device = torch.device(device)
     idx = device.index if device.index is not None else torch.cuda.current_device()
     t = _COUNTERS.get(idx)
     if t is None or t.numel() < n:
+        if t is not None:
+            _RETIRED_COUNTERS.append(t)
         with torch.inference_mode(False):
-            t = torch.zeros(max(n, 4096), dtype=torch.int32, device=torch.device("cuda", idx))
+            t = torch.zeros(max(n, 1 << 16), dtype=torch.int32,
+                            device=torch.device("cuda", idx))
         _COUNTERS[idx] = t
     return t
 
