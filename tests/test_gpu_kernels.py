@@ -382,3 +382,49 @@ def test_chunk_fused_norm(ops):
         ref = ops.rms_norm_gated(plain, zd, bf(w), 1e-6)
         assert torch.equal(p1, p2)
         assert_bf16_close(host(fused), host(ref), ulps=1, atol=1e-3)
+
+
+# ---------------------------------------------------------------------------
+# malformed cu_seqlens: flagged on the device, never read out of bounds
+# ---------------------------------------------------------------------------
+
+
+def test_conv_varlen_malformed_cu_is_flagged(ops):
+    """Sequence 1 ends before it starts: GDN_STATUS_BAD_SEQLEN is raised and its
+    slot is not touched (the other sequences run)."""
+    r = I.rng(70)
+    C, K, slots = 256, 4, 5
+    x = O.round_bf16(r.standard_normal((100, C)).astype(np.float32))
+    pool = O.round_bf16(r.standard_normal((slots, C, K - 1)).astype(np.float32))
+    w = O.round_bf16(r.uniform(-0.6, 0.6, (C, K)).astype(np.float32))
+    pool_d = bf(pool)
+    ops.check_status()
+    ops.causal_conv_silu_varlen(bf(x), pool_d, i64([0, 3, 1]), bf(w), i32([0, 50, 30, 100]))
+    with pytest.raises(ValueError):
+        ops.check_status()
+    assert np.array_equal(host(pool_d)[3], pool[3])
+
+
+@pytest.mark.parametrize("D", [128, 64])    # tensor-core and fp32 kernels
+def test_chunk_malformed_cu_is_flagged(ops, D):
+    """A sequence past the end of the rows and one longer than max_seqlen: both
+    flagged; the first is skipped (slot untouched), the second truncated."""
+    HK, HV = 1, 2
+    N = 150
+    q, k, v, g, beta = I.core_inputs(N, HK, D, HV, D, seed=71)
+    q, k, v, beta = (O.round_bf16(t) for t in (q, k, v, beta))
+    pool = (I.rng(72).standard_normal((4, HV, D, D)) * 0.02).astype(np.float32)
+    pool_d = f32(pool)
+    ops.check_status()
+    ops.chunk_gated_delta_rule_varlen(bf(q), bf(k), bf(v), f32(g), bf(beta), pool_d,
+                                      i64([0, 2]), i32([0, 100, 180]), 80)
+    with pytest.raises(ValueError):
+        ops.check_status()
+    got = host(pool_d)
+    assert np.array_equal(got[2], pool[2])            # [100, 180) runs past 150 rows: skipped
+    assert np.array_equal(got[[1, 3]], pool[[1, 3]])  # unused slots
+    # the over-long sequence is truncated to max_seqlen = 80 tokens
+    ref_pool = pool.copy()
+    O.chunk_prefill_varlen(q[:80], k[:80], v[:80], g[:80], beta[:80], ref_pool, np.array([0]),
+                           np.array([0, 80]), dtype=np.float64)
+    assert state_rel(got[0], ref_pool[0]) <= STATE_RTOL
