@@ -179,10 +179,12 @@ class DecodeStack:
                     m.out_proj.weight.normal_(0, (c["HV"] * c["DV"]) ** -0.5, generator=g)
         finally:
             torch.set_default_dtype(prev)
-        self.pools = pkg.state_pool.StatePools(self.layers, c["slots"], device)
-        with torch.no_grad():
-            self.pools.s_pool.normal_(0, 0.02, generator=g)
-            self.pools.conv_pool.normal_(0, 1.0, generator=g)
+        self.pools = None   # a pipeline stage can own no layers (ceil split, many stages)
+        if self.layers:
+            self.pools = pkg.state_pool.StatePools(self.layers, c["slots"], device)
+            with torch.no_grad():
+                self.pools.s_pool.normal_(0, 0.02, generator=g)
+                self.pools.conv_pool.normal_(0, 1.0, generator=g)
         perm = torch.randperm(c["slots"], generator=torch.Generator().manual_seed(seed))
         self.ids = perm[:c["bs"]].to(device)
         self.cu = torch.arange(c["bs"] + 1, dtype=torch.int32, device=device)
@@ -227,8 +229,9 @@ def pp_bench(pkg, dev, world, rank, steps, warmup):
     c = C1
     P = pkg.parallel
     lo, hi = P.split_layers(c["layers"], world, rank)
+    n_layers = max(0, hi - lo)   # the ceil split leaves the last stages empty at 8 stages
     prev, nxt = P.pp_peers(rank, 1, world)
-    stack = DecodeStack(pkg, dev, seed=4321 + rank, layers=hi - lo)
+    stack = DecodeStack(pkg, dev, seed=4321 + rank, layers=n_layers)
     stack.capture()
     ho = P.PipelineHandoff(c["hidden"], c["bs"], torch.bfloat16, dev, prev, nxt, mode="packed")
 
@@ -255,7 +258,9 @@ def pp_bench(pkg, dev, world, rank, steps, warmup):
     torch.cuda.synchronize()
     barrier(world)
     exposed = max(0.0, (t_pp - t_stage) / t_pp)
-    out = {"stages": world, "layers_per_stage": hi - lo,
+    per_stage = [max(0, b - a) for a, b in (P.split_layers(c["layers"], world, r)
+                                             for r in range(world))]
+    out = {"stages": world, "layers_per_stage": per_stage,
            "handoff": "PipelineHandoff packed (hidden, residual) over NCCL, side stream",
            "bytes_per_handoff": 2 * c["bs"] * c["hidden"] * 2,
            "ms_per_step_pipelined": round(t_pp / steps * 1e3, 4),
