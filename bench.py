@@ -224,8 +224,9 @@ def pp_bench(pkg, dev, world, rank, steps, warmup):
     double-buffered, ordered by events) — the reference's two blocking
     send/recv per boundary (engine/model_runner.py:795-810) replaced.  Stage r
     starts step i+1 as soon as it has sent step i, so stages overlap across
-    steps.  Exposed handoff = (pipelined step time - slowest stage's compute
-    time) / pipelined step time, both CUDA-event timed, max over ranks."""
+    steps.  Exposed handoff = (pipelined time - (K + S - 1) slowest-stage
+    compute steps) / pipelined time for K steps through S stages (the pipeline
+    fills once), CUDA-event timed, max over ranks."""
     c = C1
     P = pkg.parallel
     lo, hi = P.split_layers(c["layers"], world, rank)
@@ -257,7 +258,10 @@ def pp_bench(pkg, dev, world, rank, steps, warmup):
     ho.flush()
     torch.cuda.synchronize()
     barrier(world)
-    exposed = max(0.0, (t_pp - t_stage) / t_pp)
+    # K pipelined steps through S stages take (K + S - 1) stage-steps even with a
+    # free handoff (the pipeline fills once); what is left over is the handoff
+    fill = (world - 1) * t_stage / steps
+    exposed = max(0.0, (t_pp - t_stage - fill) / t_pp)
     per_stage = [max(0, b - a) for a, b in (P.split_layers(c["layers"], world, r)
                                              for r in range(world))]
     out = {"stages": world, "layers_per_stage": per_stage,
@@ -265,6 +269,7 @@ def pp_bench(pkg, dev, world, rank, steps, warmup):
            "bytes_per_handoff": 2 * c["bs"] * c["hidden"] * 2,
            "ms_per_step_pipelined": round(t_pp / steps * 1e3, 4),
            "ms_per_step_slowest_stage": round(t_stage / steps * 1e3, 4),
+           "pipeline_fill_ms": round(fill * 1e3, 4),
            "exposed_handoff_frac": round(exposed, 4),
            "tok_s_pipelined": round(c["bs"] * steps / t_pp, 1)}
     stack.graph = None
