@@ -243,11 +243,13 @@ __global__ void __launch_bounds__(kConvThreads) conv_varlen_kernel(
 
 // New state of sequence r = last K-1 entries of [old state | x rows]
 // (qwen3_5.py:450-456).  Launched after conv_varlen_kernel on the same stream.
+// Every sequence passes through here, so this is where a malformed one (negative
+// length, or rows outside [0, n_tokens)) is flagged; its slot is left alone.
 template <int K>
 __global__ void __launch_bounds__(kConvThreads) conv_state_writeback_kernel(
     const bf16* __restrict__ x, int64_t xs, bf16* __restrict__ pool, int64_t slot_stride,
     int64_t num_slots, const int64_t* __restrict__ ids, const int32_t* __restrict__ cu, int C,
-    int64_t n_tokens) {
+    int64_t n_tokens, int32_t* status) {
   constexpr int T = K - 1;
   const int r = blockIdx.y;
   const int c = blockIdx.x * kConvThreads + threadIdx.x;
@@ -255,7 +257,11 @@ __global__ void __launch_bounds__(kConvThreads) conv_state_writeback_kernel(
   const int64_t slot = ids[r];
   if (slot < 0 || slot >= num_slots) return;  // flagged by the conv kernel
   const int64_t start = cu[r], len = (int64_t)cu[r + 1] - start;
-  if (len <= 0 || start < 0 || start + len > n_tokens) return;  // flagged by the conv kernel
+  if (len < 0 || start < 0 || start + len > n_tokens) {
+    if (status && blockIdx.x == 0 && threadIdx.x == 0) atomicOr(status, GDN_STATUS_BAD_SEQLEN);
+    return;
+  }
+  if (len == 0) return;   // an empty sequence keeps its state
   bf16* sp = pool + slot * slot_stride + (int64_t)c * T;
   bf16 old[T], nw[T];
 #pragma unroll
@@ -355,7 +361,7 @@ extern "C" int gdn_causal_conv_silu_varlen(const void* x, int64_t x_row_stride, 
     }                                                                                            \
     conv_state_writeback_kernel<KK><<<wgrid, kConvThreads, 0, s>>>(                              \
         (const bf16*)x, x_row_stride, (bf16*)conv_pool, slot_stride, num_slots, ids, cu_seqlens, \
-        channels, n_tokens);                                                                            \
+        channels, n_tokens, status);                                                                    \
   }
   GDN_VL(2) GDN_VL(3) GDN_VL(4)
 #undef GDN_VL
