@@ -428,3 +428,96 @@ def test_chunk_malformed_cu_is_flagged(ops, D):
     O.chunk_prefill_varlen(q[:80], k[:80], v[:80], g[:80], beta[:80], ref_pool, np.array([0]),
                            np.array([0, 80]), dtype=np.float64)
     assert state_rel(got[0], ref_pool[0]) <= STATE_RTOL
+
+
+# ---------------------------------------------------------------------------
+# integer-exact probes: bit-exact slots, heads and sequence boundaries
+# ---------------------------------------------------------------------------
+#
+# g = 0 (no decay), beta = 1, k and q one-hot with magnitude 2^10 (their l2 norms
+# are exact: rsqrt(2^20 + 1e-6) = 2^-10 in fp32), v and the states small integers:
+# every product and sum of the delta rule is then exact in fp32 (and in the
+# tensor-core kernel's bf16 hi/lo operands), so the new states must equal the
+# sequential recurrence bit for bit, and each output element is one state value
+# times Dk^-1/2 rounded once.  The one-hot positions differ per token and head,
+# so a wrong slot, head (GQA mapping) or sequence boundary changes the bits.
+
+
+def _exact_recurrence(q_pos, k_pos, v, S, scale):
+    """Sequential delta rule for one-hot q/k (positions) on an integer state S
+    [D, D] (fp32, updated in place); returns the outputs [T, D] (fp32 products
+    S[j] * scale as the kernels form them, before the bf16 rounding)."""
+    outs = []
+    for t in range(len(k_pos)):
+        i, j = int(k_pos[t]), int(q_pos[t])
+        S[i, :] = v[t]                       # S[i] + (v - S[i]) with exact integers
+        outs.append(S[j, :] * np.float32(scale))
+    return np.array(outs, np.float32)
+
+
+def _onehot(pos, D):
+    x = np.zeros((len(pos), D), np.float32)
+    x[np.arange(len(pos)), pos] = 1024.0
+    return x
+
+
+def test_recurrent_integer_exact(ops):
+    HK, HV, D, slots = 2, 4, 128, 7
+    rep = HV // HK
+    r = I.rng(80)
+    bs = 3
+    ids = np.array([5, 0, 3])
+    pool = r.integers(-8, 9, (slots, HV, D, D)).astype(np.float32)    # canaries everywhere
+    qp = r.integers(0, D, (bs, HK))
+    kp = r.integers(0, D, (bs, HK))
+    q = np.stack([_onehot(qp[:, hk], D) for hk in range(HK)], 1)       # [bs, HK, D]
+    k = np.stack([_onehot(kp[:, hk], D) for hk in range(HK)], 1)
+    v = r.integers(-8, 9, (bs, HV, D)).astype(np.float32)
+    g = np.zeros((bs, HV), np.float32)
+    beta = np.ones((bs, HV), np.float32)
+    pool_d = f32(pool)
+    out = ops.recurrent_gdn_inplace(bf(q), bf(k), bf(v), f32(g), bf(beta), pool_d, i64(ids))
+    ref_pool = pool.copy()
+    ref_out = np.zeros((bs, HV, D), np.float32)
+    for b in range(bs):
+        for h in range(HV):
+            hk = h // rep
+            ref_out[b, h] = _exact_recurrence([qp[b, hk]], [kp[b, hk]], v[b, h][None],
+                                              ref_pool[ids[b], h], D ** -0.5)[0]
+    assert np.array_equal(host(pool_d), ref_pool)          # every slot, bit for bit
+    assert np.array_equal(host(out)[:, 0], O.round_bf16(ref_out))
+    ops.check_status()
+
+
+@pytest.mark.parametrize("D", [128, 64])    # tensor-core and fp32 kernels
+def test_chunk_integer_exact(ops, D):
+    HK, HV = 2, 4
+    rep = HV // HK
+    lens = [70, 1, 0, 130, 64]
+    N = sum(lens)
+    slots = len(lens) + 3
+    r = I.rng(81 + D)
+    ids = r.permutation(slots)[:len(lens)]
+    pool = r.integers(-8, 9, (slots, HV, D, D)).astype(np.float32)
+    qp = r.integers(0, D, (N, HK))
+    kp = r.integers(0, D, (N, HK))
+    q = np.stack([_onehot(qp[:, hk], D) for hk in range(HK)], 1)
+    k = np.stack([_onehot(kp[:, hk], D) for hk in range(HK)], 1)
+    v = r.integers(-8, 9, (N, HV, D)).astype(np.float32)
+    g = np.zeros((N, HV), np.float32)
+    beta = np.ones((N, HV), np.float32)
+    cu = I.cu_from_lens(lens)
+    pool_d = f32(pool)
+    out = ops.chunk_gated_delta_rule_varlen(bf(q), bf(k), bf(v), f32(g), bf(beta), pool_d,
+                                            i64(ids), i32(cu), max(lens))
+    ref_pool = pool.copy()
+    ref_out = np.zeros((N, HV, D), np.float32)
+    for s, sl in enumerate(ids):
+        t0, t1 = int(cu[s]), int(cu[s + 1])
+        for h in range(HV):
+            hk = h // rep
+            ref_out[t0:t1, h] = _exact_recurrence(qp[t0:t1, hk], kp[t0:t1, hk], v[t0:t1, h],
+                                                  ref_pool[sl, h], D ** -0.5).reshape(-1, D)
+    assert np.array_equal(host(pool_d), ref_pool)          # every slot, bit for bit
+    assert np.array_equal(host(out), O.round_bf16(ref_out))
+    ops.check_status()
