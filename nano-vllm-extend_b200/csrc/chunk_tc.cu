@@ -459,18 +459,6 @@ __global__ void __launch_bounds__(kThreads, 2) chunk_prefill_tc_kernel(
                 make_float4(p[4 * q4], p[4 * q4 + 1], p[4 * q4 + 2], p[4 * q4 + 3]);
         }
       }
-      if (isq) {   // Q row i <- e^gamma_i nq_i q_i (bf16), so MMA 3 yields the inter-chunk term
-        const __nv_bfloat162 f2 = __float2bfloat162_rn(sm.eg[i] * sm.nq[i]);
-#pragma unroll 4
-        for (int ch = 0; ch < 16; ++ch) {
-          uint4* pq = reinterpret_cast<uint4*>(sm.kq[ch >> 3] + sw128(64 + i, (ch & 7) * 8));
-          uint4 u = *pq;
-          __nv_bfloat162* hp = reinterpret_cast<__nv_bfloat162*>(&u);
-#pragma unroll
-          for (int e = 0; e < 4; ++e) hp[e] = __hmul2(hp[e], f2);
-          *pq = u;
-        }
-      }
     }
     __syncthreads();
 
@@ -519,7 +507,7 @@ __global__ void __launch_bounds__(kThreads, 2) chunk_prefill_tc_kernel(
     tmem_wait_st();
     sync_for_mma();
 
-    // ---- (3) XQ = [K; e^gamma nq Q] S : M=128, N=128, K=128 (dk); B = S rows (MN-major)
+    // ---- (3) XQ = [K; Q] S : M=128, N=128, K=128 (dk); B = S rows (MN-major)
     if (tid == 0) {
 #pragma unroll
       for (int s = 0; s < 8; ++s)
@@ -531,7 +519,21 @@ __global__ void __launch_bounds__(kThreads, 2) chunk_prefill_tc_kernel(
     if (!(ok = wait_mma())) break;
     if (c + 1 < nchunks) load_q(c + 1);   // Q rows are no longer read this chunk
 
-    // ---- R = beta (v - e^gamma nk X) -> hi / lo tiles (rows 0-63); clear those TMEM rows
+    // ---- R = beta (v - e^gamma nk X) -> hi / lo tiles (rows 0-63); clear those TMEM rows.
+    // Meanwhile the threads of rows 64-127 scale QS by e^gamma nq in TMEM (fp32), so
+    // MMA 4 adds the intra-chunk term onto the inter-chunk output.
+    if (tid >= 64) {
+      const int i = tid - 64;
+      const float f = sm.eg[i] * sm.nq[i];
+#pragma unroll
+      for (int cg = 0; cg < 4; ++cg) {
+        float x[32];
+        tmem_ld32(tl + kColW + cg * 32, x);
+#pragma unroll
+        for (int e = 0; e < 32; e += 2) fmul2(x[e], x[e + 1], x[e], x[e + 1], f, f);
+        tmem_st32(tl + kColW + cg * 32, x);
+      }
+    }
     if (tid < 64) {
       const int i = tid;
       const float xs = sm.eg[i] * sm.nk[i];
