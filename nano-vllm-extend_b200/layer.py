@@ -173,18 +173,19 @@ class Qwen3_5GatedDeltaNet(nn.Module):
             n1 = 0
             while n1 < len(lens_q) and lens_q[n1] == 1:
                 n1 += 1
-        # the gated RMSNorm (self.norm) runs fused in each core's kernels
-        outs = []
+        # the gated RMSNorm (self.norm) runs fused in each core's kernels; decode and
+        # prefill rows write their halves of one output buffer (no concatenation)
+        core = torch.empty(N, hv, self.head_v_dim, dtype=torch.bfloat16,
+                           device=hidden_states.device)
         if n1:
-            outs.append(self._decode_core(mixed[:n1], z[:n1], b[:n1], a[:n1], ids[:n1]))
+            self._decode_core(mixed[:n1], z[:n1], b[:n1], a[:n1], ids[:n1], out=core[:n1])
         if n1 < N:
             cu_q = ctx.cu_seqlens_q
             cu_p = cu_q[n1:] - cu_q[n1] if n1 else cu_q
             g, beta = ops.fused_g_beta(b[n1:], a[n1:], self.A_log[self._v_head_slice],
                                        self.dt_bias[self._v_head_slice], None)
-            outs.append(self._prefill_core(mixed[n1:], g, beta, ids[n1:], cu_p,
-                                           max(lens_q[n1:]), z[n1:]))
-        core = outs[0] if len(outs) == 1 else torch.cat(outs, 0)    # [N, HV, DV], normed
+            self._prefill_core(mixed[n1:], g, beta, ids[n1:], cu_p, max(lens_q[n1:]), z[n1:],
+                               out=core[n1:])
         return self.out_proj(core.view(N, vd))
 
     def _split(self, y: torch.Tensor):
@@ -195,7 +196,7 @@ class Qwen3_5GatedDeltaNet(nn.Module):
         v = y[:, 2 * kd:].view(n, self.num_v_heads, self.head_v_dim)
         return q, k, v
 
-    def _decode_core(self, mixed, z, b, a, ids):
+    def _decode_core(self, mixed, z, b, a, ids, out=None):
         """T == 1 rows: conv step + gate + in-place recurrent + gated norm
         (qwen3_5.py:976-982, 1008-1026, 1083-1085), one fused kernel when the
         shape allows (``fused_decode``), else the four operators."""
@@ -205,15 +206,19 @@ class Qwen3_5GatedDeltaNet(nn.Module):
         if self.fused_decode and ops.decode_fused_supported(self.num_k_heads, self.num_v_heads,
                                               self.head_k_dim, self.head_v_dim, self.conv_kernel):
             return ops.decode_fused(mixed, z, b, a, self.conv_cache, w, a_log, dt_bias,
-                                    self.s_cache, ids, self.norm.weight, self.norm.eps)
+                                    self.s_cache, ids, self.norm.weight, self.norm.eps, out=out)
         g, beta = ops.fused_g_beta(b, a, a_log, dt_bias, None)
         y = ops.conv_decode_step(mixed, self.conv_cache, ids, w)
         q, k, v = self._split(y)
         o = ops.recurrent_gdn_inplace(q, k, v, g, beta, self.s_cache, ids, z=z,
                                       norm_weight=self.norm.weight, eps=self.norm.eps)
-        return o.view(-1, self.num_v_heads, self.head_v_dim)
+        o = o.view(-1, self.num_v_heads, self.head_v_dim)
+        if out is not None:
+            out.copy_(o)
+            return out
+        return o
 
-    def _prefill_core(self, mixed, g, beta, ids, cu_seqlens, max_seqlen, z):
+    def _prefill_core(self, mixed, g, beta, ids, cu_seqlens, max_seqlen, z, out=None):
         """Prefill rows: varlen conv + chunked rule with slot states + gated
         norm (the composition of qwen3_5.py:922-963, unpadded)."""
         y = ops.causal_conv_silu_varlen(mixed, self.conv_cache, ids,
@@ -222,7 +227,7 @@ class Qwen3_5GatedDeltaNet(nn.Module):
         q, k, v = self._split(y)
         return ops.chunk_gated_delta_rule_varlen(q, k, v, g, beta, self.s_cache, ids, cu_seqlens,
                                                  max_seqlen, z=z, norm_weight=self.norm.weight,
-                                                 eps=self.norm.eps)
+                                                 eps=self.norm.eps, out=out)
 
 
 def install(qwen3_5_module=None, parallel_module=None, context_module=None):

@@ -56,6 +56,17 @@ def check_status(device=None, clear: bool = True) -> int:
     return v
 
 
+def _out_buffer(out, shape, device) -> torch.Tensor:
+    """A bf16 output of `shape`: `out` itself when given (a contiguous tensor of
+    that shape, e.g. a row slice of a larger buffer), else a new tensor."""
+    if out is None:
+        return torch.empty(*shape, dtype=torch.bfloat16, device=device)
+    assert tuple(out.shape) == tuple(shape) and out.dtype == torch.bfloat16 and \
+        out.is_contiguous() and out.device == torch.device(device), \
+        f"out must be a contiguous bf16 tensor of shape {tuple(shape)}"
+    return out
+
+
 def _p(t) -> int:
     return 0 if t is None else t.data_ptr()
 
@@ -265,7 +276,7 @@ def recurrent_gdn_inplace(q, k, v, g, beta, s_pool, ids, z=None, norm_weight=Non
 
 def chunk_gated_delta_rule_varlen(q, k, v, g, beta, s_pool, ids, cu_seqlens,
                                   max_seqlen: int, z=None, norm_weight=None,
-                                  eps: float = 1e-6) -> torch.Tensor:
+                                  eps: float = 1e-6, out=None) -> torch.Tensor:
     """Varlen chunked prefill (the chunk rule of qwen3_5.py:140-227 driven by
     cu_seqlens as at :956-961), initial state read from and final state
     written to ``s_pool[ids[r]]``.  q/k [N, HK, DK], v [N, HV, DV] (row
@@ -286,7 +297,7 @@ def chunk_gated_delta_rule_varlen(q, k, v, g, beta, s_pool, ids, cu_seqlens,
         else cu_seqlens.contiguous()
     assert cu.numel() == ids.numel() + 1
     z3, zs, nw = _norm_args(z, norm_weight, N, HV, DV)
-    out = torch.empty(N, HV, DV, dtype=v.dtype, device=v.device)
+    out = _out_buffer(out, (N, HV, DV), v.device)
     rc = _lib.load().gdn_chunk_prefill_varlen(
         _p(q), qs, _p(k), ks, _p(v), vs, _p(g), _p(beta), _p(s_pool), _slot_stride(s_pool),
         s_pool.shape[0], _p(ids), _p(cu), ids.numel(), N, int(max_seqlen), _p(out), HK, HV, DK,
@@ -362,7 +373,7 @@ def decode_fused(mixed: torch.Tensor, z: torch.Tensor, b: torch.Tensor, a: torch
                  conv_pool: torch.Tensor, conv_weight: torch.Tensor, a_log: torch.Tensor,
                  dt_bias: torch.Tensor, s_pool: torch.Tensor, ids: torch.Tensor,
                  norm_weight: torch.Tensor, eps: float = 1e-6,
-                 counters: bool = True) -> torch.Tensor:
+                 counters: bool = True, out=None) -> torch.Tensor:
     """The decode branch of Qwen3_5GatedDeltaNet.forward for T == 1 rows in one
     kernel: conv_decode_step (qwen3_5.py:1008-1012) + fused_g_beta (:976-982)
     + recurrent_gdn_inplace (:1013-1026) + the gated norm (:1083-1085).
@@ -400,7 +411,7 @@ def decode_fused(mixed: torch.Tensor, z: torch.Tensor, b: torch.Tensor, a: torch
     ids = _ids64(ids)
     assert ids.numel() == bs
     assert conv_pool.shape[0] == s_pool.shape[0], "both pools index the same slots"
-    out = torch.empty(bs, HV, D, dtype=torch.bfloat16, device=mixed.device)
+    out = _out_buffer(out, (bs, HV, D), mixed.device)
     cnt = group_counters(mixed.device, bs * HK) if counters else None
     rc = _lib.load().gdn_decode_fused(
         _p(m2), ms, _p(z3), zs, _p(b), _p(a), b.stride(0), _p(conv_pool), _slot_stride(conv_pool),
