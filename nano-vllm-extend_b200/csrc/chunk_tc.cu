@@ -1,9 +1,9 @@
 // (c) Chunked gated-delta-rule prefill on tcgen05 tensor cores (sm_100a).
 //
-// One CTA (256 threads; warps w and w+4 read TMEM lanes 32(w%4).. and split
-// the columns) walks one (sequence, v-head) chain chunk by chunk (64 tokens).  The fp32 state S [dk x dv] lives
-// in TMEM for the whole sequence: read from the pool slot at the start,
-// written back at the end.  With q^ = l2norm(q)*scale, k^ = l2norm(k),
+// One CTA (128 threads, thread t <-> TMEM lane t; two CTAs per SM) walks one
+// (sequence, v-head) chain chunk by chunk (64 tokens), the chains launched
+// longest first.  The fp32 state S [dk x dv] lives in TMEM for the whole
+// sequence: read from the pool slot at the start, written back at the end.  With q^ = l2norm(q)*scale, k^ = l2norm(k),
 // gamma = in-chunk cumsum(g) (qwen3_5.py:152-227), every chunk runs five
 // M = 128 MMAs (bf16 operands from 128B-swizzled shared memory, fp32
 // accumulators in TMEM):
