@@ -265,6 +265,10 @@ extern "C" int gdn_chunk_prefill_varlen(const void* q, int64_t q_row_stride, con
                                 z_row_stride >= (int64_t)num_v_heads * head_v_dim),
               "gdn_chunk_prefill_varlen: fused norm needs norm_weight and z rows of HV*DV");
   if (n_seqs == 0 || n_tokens == 0) return GDN_OK;
+  // token rows are int32 TMA coordinates and (sequence, head) chains one CTA each
+  GDN_UNSUPPORTED(n_tokens < (1ll << 31) && (int64_t)n_seqs * num_v_heads < (1ll << 31),
+                  "gdn_chunk_prefill_varlen: %lld tokens / %lld chains exceed 2^31",
+                  (long long)n_tokens, (long long)n_seqs * num_v_heads);
   GDN_REQUIRE(q && k && v && g && beta && s_pool && ids && cu_seqlens && out,
               "gdn_chunk_prefill_varlen: null pointer");
   cudaStream_t s = (cudaStream_t)stream;
