@@ -462,6 +462,8 @@ def prefill_bench(pkg, device, steps, peaks):
                 torch.cuda.synchronize()
         pkg.ops.chunk_gated_delta_rule_varlen(q, k, v, gg, beta, m.s_cache, ids, cu, max(lens))
         torch.cuda.synchronize()
+        clocks = Clocks(device.index if device.index is not None else 0)
+        clocks.start()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record()
         for _ in range(steps):
@@ -469,6 +471,7 @@ def prefill_bench(pkg, device, steps, peaks):
                                                   max(lens))
         e1.record()
         torch.cuda.synchronize()
+        chunk_clk = clocks.stop()
         o = pkg.ops.chunk_gated_delta_rule_varlen(q, k, v, gg, beta, m.s_cache, ids, cu,
                                                   max(lens))
         pkg.ops.rms_norm_gated(o, z, m.norm.weight, 1e-6)
@@ -498,7 +501,7 @@ def prefill_bench(pkg, device, steps, peaks):
                              "achieved": round(achieved, 2), "unit": "TFLOP/s",
                              "peak": peaks["bf16_tflops"], "peak_source": peaks["source"],
                              "frac": round(achieved / peaks["bf16_tflops"], 5),
-                             "algorithmic_flops": flops}}
+                             "algorithmic_flops": flops, "clocks": chunk_clk}}
 
 
 # ---------------------------------------------------------------------------
