@@ -38,7 +38,7 @@
 extern "C" {
 #endif
 
-#define GDN_ABI_VERSION 4
+#define GDN_ABI_VERSION 5
 
 enum gdn_status_code {
   GDN_OK = 0,
@@ -162,7 +162,19 @@ int gdn_recurrent_inplace(const void* q, int64_t q_row_stride,
  * Chunk size 64, as the reference.  Supported head dims and the optional
  * gated-RMSNorm epilogue (z, z_row_stride, norm_weight, norm_eps) as
  * gdn_recurrent_inplace.
+ *
+ * workspace: optional device scratch of at least
+ * gdn_chunk_prefill_workspace_bytes(n_tokens, n_seqs, num_v_heads, ...) bytes,
+ * 16-byte aligned, used only during the call (stream-ordered).  With it, head
+ * dim 128 runs the split form: the state-independent factors of every chunk
+ * in a parallel pass, then the serial chain per (sequence, head).  NULL runs
+ * the one-kernel form.  Both give the same bits.  A non-NULL workspace that is
+ * too small is GDN_ERR_INVALID_ARGUMENT.  The reference allocates its chunk
+ * intermediates inside the call; here the caller does.
  */
+int64_t gdn_chunk_prefill_workspace_bytes(int64_t n_tokens, int32_t n_seqs, int32_t num_v_heads,
+                                          int32_t head_k_dim, int32_t head_v_dim);
+
 int gdn_chunk_prefill_varlen(const void* q, int64_t q_row_stride,
                              const void* k, int64_t k_row_stride,
                              const void* v, int64_t v_row_stride,
@@ -173,7 +185,8 @@ int gdn_chunk_prefill_varlen(const void* q, int64_t q_row_stride,
                              void* out, int32_t num_k_heads, int32_t num_v_heads,
                              int32_t head_k_dim, int32_t head_v_dim, float scale,
                              const void* z, int64_t z_row_stride, const void* norm_weight,
-                             float norm_eps, int32_t* status, void* stream);
+                             float norm_eps, void* workspace, int64_t workspace_bytes,
+                             int32_t* status, void* stream);
 
 /*
  * Gated RMSNorm over the value head dim.  Replaces Qwen3_5RMSNormGated /

@@ -35,8 +35,10 @@ SIGNATURES = {
                                     i64, vp, vp],
     "gdn_recurrent_inplace": [vp, i64, vp, i64, vp, i64, vp, vp, vp, i64, i64, vp, vp, i32, i32,
                               i32, i32, i32, f32, vp, i64, vp, f32, vp, vp],
+    "gdn_chunk_prefill_workspace_bytes": [i64, i32, i32, i32, i32],
     "gdn_chunk_prefill_varlen": [vp, i64, vp, i64, vp, i64, vp, vp, vp, i64, i64, vp, vp, i32,
-                                 i64, i32, vp, i32, i32, i32, i32, f32, vp, i64, vp, f32, vp, vp],
+                                 i64, i32, vp, i32, i32, i32, i32, f32, vp, i64, vp, f32, vp, i64,
+                                 vp, vp],
     "gdn_rms_norm_gated": [vp, vp, i64, i32, vp, vp, i64, i32, f32, vp],
     "gdn_decode_fused": [vp, i64, vp, i64, vp, vp, i64, vp, i64, vp, i32, vp, vp, i32, vp, i64,
                          i64, vp, vp, f32, vp, i32, i32, i32, i32, f32, vp, vp, vp],
@@ -60,7 +62,8 @@ def load() -> C.CDLL:
     for name, argtypes in SIGNATURES.items():
         fn = getattr(lib, name)
         fn.argtypes = argtypes
-        fn.restype = C.c_char_p if name == "gdn_last_error" else C.c_int
+        fn.restype = {"gdn_last_error": C.c_char_p,
+                      "gdn_chunk_prefill_workspace_bytes": C.c_int64}.get(name, C.c_int)
     _LIB = lib
     return lib
 

@@ -229,6 +229,13 @@ int chunk_prefill_tc(int n_seqs, int HV, cudaStream_t s, const bf16* q, int64_t 
                      const int64_t* ids, const int32_t* cu, int64_t n_tokens, int max_seqlen,
                      bf16* out, int HK, float scale, const bf16* z, int64_t zs, const bf16* nw,
                      float eps, int32_t* status);
+int64_t chunk_wy_capacity(int64_t n_tokens, int64_t n_seqs);
+int64_t chunk_wy_workspace_bytes(int64_t n_tokens, int64_t n_seqs, int64_t HV);
+int chunk_prefill_wy(int n_seqs, int HV, cudaStream_t s, const bf16* q, int64_t qs,
+                     const bf16* k, int64_t ks, const bf16* v, int64_t vs, const float* g,
+                     const bf16* beta, float* pool, int64_t slot_stride, int64_t num_slots,
+                     const int64_t* ids, const int32_t* cu, int64_t n_tokens, int max_seqlen,
+                     bf16* out, int HK, float scale, void* workspace, int32_t* status);
 
 }  // namespace gdn
 
@@ -244,6 +251,7 @@ extern "C" int gdn_chunk_prefill_varlen(const void* q, int64_t q_row_stride, con
                                         int32_t head_k_dim, int32_t head_v_dim, float scale,
                                         const void* z, int64_t z_row_stride,
                                         const void* norm_weight, float norm_eps,
+                                        void* workspace, int64_t workspace_bytes,
                                         int32_t* status, void* stream) {
   clear_error();
   GDN_REQUIRE(n_seqs >= 0 && n_tokens >= 0 && max_seqlen >= 0 && num_k_heads > 0 &&
@@ -272,8 +280,29 @@ extern "C" int gdn_chunk_prefill_varlen(const void* q, int64_t q_row_stride, con
   GDN_REQUIRE(q && k && v && g && beta && s_pool && ids && cu_seqlens && out,
               "gdn_chunk_prefill_varlen: null pointer");
   cudaStream_t s = (cudaStream_t)stream;
-  if (chunk_tc_supported(head_k_dim, q, q_row_stride, k, k_row_stride, v, v_row_stride, out,
-                         s_pool, slot_stride, z, z_row_stride, norm_weight))
+  const bool tc = chunk_tc_supported(head_k_dim, q, q_row_stride, k, k_row_stride, v,
+                                     v_row_stride, out, s_pool, slot_stride, z, z_row_stride,
+                                     norm_weight);
+  if (tc && workspace != nullptr) {
+    const int64_t need = chunk_wy_workspace_bytes(n_tokens, n_seqs, num_v_heads);
+    GDN_REQUIRE(workspace_bytes >= need && aligned16(workspace),
+                "gdn_chunk_prefill_varlen: workspace of %lld bytes (16-byte aligned) needed, "
+                "got %lld", (long long)need, (long long)workspace_bytes);
+    // (chunk, head) blocks are numbered by int32 and launched one CTA each
+    GDN_UNSUPPORTED(chunk_wy_capacity(n_tokens, n_seqs) * num_v_heads < (1ll << 31),
+                    "gdn_chunk_prefill_varlen: %lld chunk blocks exceed 2^31",
+                    (long long)(chunk_wy_capacity(n_tokens, n_seqs) * num_v_heads));
+    int rc = chunk_prefill_wy(n_seqs, num_v_heads, s, (const bf16*)q, q_row_stride,
+                              (const bf16*)k, k_row_stride, (const bf16*)v, v_row_stride, g,
+                              (const bf16*)beta, s_pool, slot_stride, num_slots, ids, cu_seqlens,
+                              n_tokens, max_seqlen, (bf16*)out, num_k_heads, scale, workspace,
+                              status);
+    if (rc == GDN_OK && z != nullptr)
+      rc = launch_rms_norm_gated(out, z, z_row_stride, num_v_heads, norm_weight, out,
+                                 n_tokens * num_v_heads, head_v_dim, norm_eps, s);
+    return rc;
+  }
+  if (tc)
     return chunk_prefill_tc(n_seqs, num_v_heads, s, (const bf16*)q, q_row_stride, (const bf16*)k,
                             k_row_stride, (const bf16*)v, v_row_stride, g, (const bf16*)beta,
                             s_pool, slot_stride, num_slots, ids, cu_seqlens, n_tokens, max_seqlen,
@@ -287,4 +316,12 @@ extern "C" int gdn_chunk_prefill_varlen(const void* q, int64_t q_row_stride, con
     rc = launch_rms_norm_gated(out, z, z_row_stride, num_v_heads, norm_weight, out,
                                n_tokens * num_v_heads, head_v_dim, norm_eps, s);
   return rc;
+}
+
+extern "C" int64_t gdn_chunk_prefill_workspace_bytes(int64_t n_tokens, int32_t n_seqs,
+                                                     int32_t num_v_heads, int32_t head_k_dim,
+                                                     int32_t head_v_dim) {
+  if (n_tokens <= 0 || n_seqs <= 0 || num_v_heads <= 0 || head_k_dim != 128 || head_v_dim != 128)
+    return 0;
+  return chunk_wy_workspace_bytes(n_tokens, n_seqs, num_v_heads);
 }

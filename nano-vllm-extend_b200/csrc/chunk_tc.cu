@@ -36,17 +36,11 @@
 // it never overflows and needs ~5x fewer exponentials than the direct form.
 // Every mbarrier wait is bounded; on timeout the CTA sets GDN_STATUS_TIMEOUT,
 // frees its TMEM and returns.
-#include <cuda.h>
-
-#include "tc_util.cuh"
-#include "tmap.cuh"
+#include "chunk_common.cuh"
 
 namespace gdn {
 namespace tc {
 
-constexpr int kC = 64;
-constexpr int kD = 128;
-constexpr int kLptMaxSeqs = 256;   // longest-first chain order up to this many sequences
 constexpr int kThreads = 128;
 constexpr uint32_t kSpin = 1u << 22;
 constexpr uint32_t kTmemCols = 256;
@@ -63,136 +57,12 @@ struct __align__(1024) ChunkSmem {
   uint8_t qkm[64 * 128];      // QKm rows 0-63; MMA 2's rows 64-127 read a4's first rows
   uint8_t a4[128 * 128];      // [T ; M2] : row x 64 tokens
   uint8_t v[2][64 * 128];     // [dv block][token row][128 B] (128B-swizzled, as TMA writes)
-  float gam[kC], eg[kC], bet[kC], nk[kC], nq[kC], bcol[kC], cf[kC], gend[4];
+  ChunkScalars sc;
   unsigned long long mbar;    // MMA completion
   unsigned long long lbar[3]; // TMA loads: K, Q, V
   uint32_t tmem_base;
   int abort;
 };
-
-__device__ __forceinline__ void st8(uint8_t* tile, uint32_t row, uint32_t col, const float* f) {
-  *reinterpret_cast<uint4*>(tile + sw128(row, col)) = pack8(f);
-}
-
-// x = hi + lo exactly: hi = x truncated to bf16 (upper 16 bits), lo = the
-// remainder rounded to bf16 (|lo| < 2^-7 |x|, so hi + lo carries ~16 bits).
-__device__ __forceinline__ void split8(const float* x, uint8_t* tile_hi, uint8_t* tile_lo,
-                                       uint32_t off) {
-  uint4 h, l;
-  uint32_t* hp = reinterpret_cast<uint32_t*>(&h);
-  __nv_bfloat162* lp = reinterpret_cast<__nv_bfloat162*>(&l);
-#pragma unroll
-  for (int e = 0; e < 4; ++e) {
-    const uint32_t b0 = __float_as_uint(x[2 * e]), b1 = __float_as_uint(x[2 * e + 1]);
-    hp[e] = __byte_perm(b0, b1, 0x7632);
-    lp[e] = __floats2bfloat162_rn(x[2 * e] - __uint_as_float(b0 & 0xFFFF0000u),
-                                  x[2 * e + 1] - __uint_as_float(b1 & 0xFFFF0000u));
-  }
-  *reinterpret_cast<uint4*>(tile_hi + off) = h;
-  *reinterpret_cast<uint4*>(tile_lo + off) = l;
-}
-
-__device__ __forceinline__ void fma4(float (&acc)[4], float a, const float4& b) {
-  ffma2(acc[0], acc[1], a, a, b.x, b.y, acc[0], acc[1]);
-  ffma2(acc[2], acc[3], a, a, b.z, b.w, acc[2], acc[3]);
-}
-
-constexpr int kLP = kC + 4;   // row pitch of L / T (16-byte aligned rows)
-
-// T = (I - L)^-1 for the strictly lower 64x64 L (fp32, shared memory, upper
-// triangle zero), computed IN PLACE (T overwrites L): 16x16 diagonal blocks by
-// forward substitution in registers, then two recursive-doubling levels —
-// with (I - L) = [A 0; -L21 B], T = [A^-1 0; B^-1 L21 A^-1  B^-1] — at
-// 16 -> 32 and 32 -> 64.  Each level reads its L21 block before the T21 that
-// replaces it is written.  128 threads; X is a 4 KiB fp32 scratch.
-__device__ __forceinline__ void invert_unit_lower(float (*LT)[kLP], float* X, int tid) {
-  const int warp = tid >> 5, lane = tid & 31;
-  {  // diagonal 16x16 blocks: warp w owns block w, lane l solves column l % 16
-    const int b0 = 16 * warp, j = lane & 15;
-    float t[16];
-#pragma unroll
-    for (int i = 0; i < 16; ++i) {
-      float s0 = 0.f, s1 = 0.f;
-#pragma unroll
-      for (int m = 0; m < i; ++m) {
-        const float pr = LT[b0 + i][b0 + m] * t[m];
-        if (m & 1) s1 += pr; else s0 += pr;
-      }
-      t[i] = (i == j) ? 1.f : (i > j ? s0 + s1 : 0.f);
-    }
-    __syncwarp();
-    if (lane < 16) {
-#pragma unroll
-      for (int i = 0; i < 16; ++i) LT[b0 + i][b0 + j] = t[i];
-    }
-  }
-  __syncthreads();
-  {  // 16 -> 32: for both 32-blocks, X = L21 A^-1, then T21 = B^-1 X (4 outputs / thread)
-    const int hsel = tid >> 6, hb = hsel * 32, r = (tid >> 2) & 15, c0 = (tid & 3) * 4;
-    float* Xh = X + hsel * 256;
-    float a[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-    for (int s = 0; s < 16; ++s)
-      fma4(a, LT[hb + 16 + r][hb + s], *reinterpret_cast<const float4*>(&LT[hb + s][hb + c0]));
-    *reinterpret_cast<float4*>(&Xh[r * 16 + c0]) = make_float4(a[0], a[1], a[2], a[3]);
-    __syncthreads();
-    float b[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-    for (int s = 0; s < 16; ++s)
-      fma4(b, LT[hb + 16 + r][hb + 16 + s], *reinterpret_cast<const float4*>(&Xh[s * 16 + c0]));
-    *reinterpret_cast<float4*>(&LT[hb + 16 + r][hb + c0]) = make_float4(b[0], b[1], b[2], b[3]);
-  }
-  __syncthreads();
-  {  // 32 -> 64: X = L21 A^-1 (32x32), then T21 = B^-1 X (8 outputs / thread)
-    const int rr = tid >> 2, c0 = (tid & 3) * 8;
-    float a0[4] = {0.f, 0.f, 0.f, 0.f}, a1[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll 8
-    for (int s = 0; s < 32; ++s) {
-      const float l = LT[32 + rr][s];
-      fma4(a0, l, *reinterpret_cast<const float4*>(&LT[s][c0]));
-      fma4(a1, l, *reinterpret_cast<const float4*>(&LT[s][c0 + 4]));
-    }
-    *reinterpret_cast<float4*>(&X[rr * 32 + c0]) = make_float4(a0[0], a0[1], a0[2], a0[3]);
-    *reinterpret_cast<float4*>(&X[rr * 32 + c0 + 4]) = make_float4(a1[0], a1[1], a1[2], a1[3]);
-    __syncthreads();
-    float b0[4] = {0.f, 0.f, 0.f, 0.f}, b1[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll 8
-    for (int s = 0; s < 32; ++s) {
-      const float t = LT[32 + rr][32 + s];
-      fma4(b0, t, *reinterpret_cast<const float4*>(&X[s * 32 + c0]));
-      fma4(b1, t, *reinterpret_cast<const float4*>(&X[s * 32 + c0 + 4]));
-    }
-    *reinterpret_cast<float4*>(&LT[32 + rr][c0]) = make_float4(b0[0], b0[1], b0[2], b0[3]);
-    *reinterpret_cast<float4*>(&LT[32 + rr][c0 + 4]) = make_float4(b1[0], b1[1], b1[2], b1[3]);
-  }
-  __syncthreads();
-}
-
-// Longest chains first: CTA rank k (of n_seqs) takes the sequence with the
-// k-th largest length (ties by index), so the long serial chains start in the
-// first wave and the short ones fill in behind them.  The ranks form a
-// permutation for any cu_seqlens, malformed ones included.  Kept out of line so
-// it does not weigh on the main loop's register allocation.
-__device__ __noinline__ int lpt_sequence(const int32_t* __restrict__ cu, int n_seqs, int rank,
-                                         int tid) {
-  __shared__ int s_len[kLptMaxSeqs];
-  __shared__ int s_seq;
-  if (n_seqs > kLptMaxSeqs) return rank;
-  for (int i = tid; i < n_seqs; i += kThreads) s_len[i] = cu[i + 1] - cu[i];
-  if (tid == 0) s_seq = rank;
-  __syncthreads();
-  for (int i = tid; i < n_seqs; i += kThreads) {
-    const int li = s_len[i];
-    int rk = 0;
-    for (int j = 0; j < n_seqs; ++j) {
-      const int lj = s_len[j];
-      rk += (lj > li) || (lj == li && j < i);
-    }
-    if (rk == rank) s_seq = i;
-  }
-  __syncthreads();
-  return s_seq;
-}
 
 __global__ void __launch_bounds__(kThreads, 2) chunk_prefill_tc_kernel(
     const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
@@ -209,7 +79,7 @@ __global__ void __launch_bounds__(kThreads, 2) chunk_prefill_tc_kernel(
   const int rank = blockIdx.x / HV;
   const int h = blockIdx.x - rank * HV;
   const int hk = h / (HV / HK);
-  const int r = lpt_sequence(cu, gridDim.x / HV, rank, tid);
+  const int r = lpt_sequence<kThreads>(cu, gridDim.x / HV, rank, tid);
 
   const int64_t slot = ids[r];
   if (!slot_ok(slot, num_slots, status)) return;
@@ -290,18 +160,19 @@ __global__ void __launch_bounds__(kThreads, 2) chunk_prefill_tc_kernel(
   const uint32_t tl = tbase + ((uint32_t)(warp * 32) << 16);   // this warp's lane window
   uint32_t phase = 0;
 
+  // One thread waits on each barrier; the others wait at the CTA barrier
+  // that follows (no issue slots spent polling).
   auto wait_mma = [&]() -> bool {
-    const bool ok = mbar_wait(bar, phase, kSpin);
-    phase ^= 1u;
-    if (!ok) {
+    if (tid == 0 && !mbar_wait(bar, phase, kSpin)) {
       sm.abort = 1;
       if (status) atomicOr(status, GDN_STATUS_TIMEOUT);
     }
-    fence_after();
+    phase ^= 1u;
     __syncthreads();
+    fence_after();
     return sm.abort == 0;
   };
-  auto wait_load = [&](int i) {     // bounded wait for TMA load i (0 K, 1 Q, 2 V)
+  auto wait_load = [&](int i) {     // TMA load i (0 K, 1 Q, 2 V); thread 0, a CTA barrier follows
     if (!mbar_wait(smem_u32(&sm.lbar[i]), lphase[i], kSpin)) {
       sm.abort = 1;
       if (status) atomicOr(status, GDN_STATUS_TIMEOUT);
@@ -344,14 +215,17 @@ __global__ void __launch_bounds__(kThreads, 2) chunk_prefill_tc_kernel(
   for (int c = 0; c < nchunks && ok; ++c) {
     const int64_t t0 = start + (int64_t)c * kC;
     const int nv = (int)min((int64_t)kC, len - (int64_t)c * kC);
-    wait_load(0);
-    wait_load(1);
-    wait_load(2);
+    if (tid == 0) {
+      wait_load(0);
+      wait_load(1);
+      wait_load(2);
+    }
     if (tid < kC) {
-      sm.gam[tid] = g_next;
-      sm.bet[tid] = __bfloat162float(__ushort_as_bfloat16(b_next));
+      sm.sc.gam[tid] = g_next;
+      sm.sc.bet[tid] = __bfloat162float(__ushort_as_bfloat16(b_next));
     }
     if (nv < kC) {   // clear rows past the sequence end in the K, Q and v tiles
+      __syncthreads();
       for (int idx = tid; idx < (kC - nv) * 16; idx += kThreads) {
         const int i = nv + idx / 16, ch = idx % 16, blk = ch >> 3, c8 = (ch & 7) * 8;
         const uint4 z = make_uint4(0, 0, 0, 0);
@@ -362,26 +236,7 @@ __global__ void __launch_bounds__(kThreads, 2) chunk_prefill_tc_kernel(
     }
     __syncthreads();
     if (sm.abort) { ok = false; break; }
-    if (warp == 0) {   // cumulative decay (inclusive scan, 2 tokens per lane) and its factors
-      const float ga = sm.gam[2 * lane], gb = sm.gam[2 * lane + 1];
-      float s = ga + gb;
-#pragma unroll
-      for (int o = 1; o < 32; o <<= 1) {
-        const float y = __shfl_up_sync(0xffffffffu, s, o);
-        if (lane >= o) s += y;
-      }
-      const float g0 = s - gb;                      // gamma of token 2*lane
-      // gamma at the end of each 16-token block (token 16J+15 = lane 8J+7, second element)
-      const float gE = __shfl_sync(0xffffffffu, s, ((2 * lane) >> 4) * 8 + 7);
-      __syncwarp();
-      sm.gam[2 * lane] = g0;
-      sm.gam[2 * lane + 1] = s;
-      sm.eg[2 * lane] = expf(g0);
-      sm.eg[2 * lane + 1] = expf(s);
-      sm.bcol[2 * lane] = __expf(gE - g0);          // <= 1 (g <= 0)
-      sm.bcol[2 * lane + 1] = __expf(gE - s);
-      if ((lane & 7) == 7) sm.gend[lane >> 3] = s;
-    }
+    if (warp == 0) decay_scan(sm.sc, lane);   // cumulative decay and its factors
     sync_for_mma();
 
     // ---- (1) P = [K;Q] [K;Q]^T : M=128, N=128, K=128 (dk); diag gives the norms
@@ -395,71 +250,11 @@ __global__ void __launch_bounds__(kThreads, 2) chunk_prefill_tc_kernel(
       mma_commit(bar);
     }
     if (!(ok = wait_mma())) break;
-    {   // norms: P[t][t] sits in this warp's 32-column diagonal window
-      float p[32];
-      tmem_ld32(tl + kColW + warp * 32, p);
-      float d = 0.f;
-#pragma unroll
-      for (int jj = 0; jj < 32; ++jj) d = (jj == lane) ? p[jj] : d;
-      if (tid < 64) {
-        const float n = rsqrtf(d + 1e-6f);
-        sm.nk[tid] = n;
-        sm.cf[tid] = n * sm.bcol[tid];
-      } else {
-        sm.nq[tid - 64] = rsqrtf(d + 1e-6f) * scale;
-      }
-    }
+    norms_from_diag(sm.sc, tl, kColW, tid, scale);   // P[t][t]: the row norms
     __syncthreads();
 
     // ---- L (rows 0-63) and QKm (rows 64-127) from P; then scale Q rows by e^gamma nq
-    {
-      const int i = tid & 63;
-      const bool isq = tid >= 64;
-      const int I = i >> 4;
-      const float gi = sm.gam[i];
-      const float rowf = isq ? sm.nq[i] : -sm.bet[i] * sm.nk[i];
-#pragma unroll
-      for (int hh = 0; hh < 2; ++hh) {
-        float p[32];
-        tmem_ld32(tl + kColW + hh * 32, p);
-#pragma unroll
-        for (int b2 = 0; b2 < 2; ++b2) {
-          const int J = hh * 2 + b2;
-          float* pe = p + b2 * 16;
-          if (J < I) {
-            // left of the diagonal block: e^(gamma_i - gamma_j) =
-            // e^(gamma_i - gamma_end(J)) * e^(gamma_end(J) - gamma_j), both <= 1
-            const float rf = rowf * __expf(gi - sm.gend[J]);
-#pragma unroll
-            for (int jj = 0; jj < 16; jj += 2) {
-              const float2 c2 = *reinterpret_cast<const float2*>(&sm.cf[J * 16 + jj]);
-              float f0, f1;
-              fmul2(f0, f1, rf, rf, c2.x, c2.y);
-              fmul2(pe[jj], pe[jj + 1], pe[jj], pe[jj + 1], f0, f1);
-            }
-          } else if (J == I) {
-#pragma unroll
-            for (int jj = 0; jj < 16; ++jj) {
-              const int j = J * 16 + jj;
-              const bool keep = isq ? (j <= i) : (j < i);
-              pe[jj] = keep ? pe[jj] * rowf * sm.nk[j] * __expf(gi - sm.gam[j]) : 0.f;
-            }
-          } else {
-#pragma unroll
-            for (int jj = 0; jj < 16; ++jj) pe[jj] = 0.f;
-          }
-        }
-        if (isq) {
-#pragma unroll
-          for (int q8 = 0; q8 < 4; ++q8) st8(sm.qkm, i, hh * 32 + q8 * 8, p + q8 * 8);
-        } else {
-#pragma unroll
-          for (int q4 = 0; q4 < 8; ++q4)
-            *reinterpret_cast<float4*>(&Lm[i][hh * 32 + q4 * 4]) =
-                make_float4(p[4 * q4], p[4 * q4 + 1], p[4 * q4 + 2], p[4 * q4 + 3]);
-        }
-      }
-    }
+    build_l_qkm(sm.sc, tl, kColW, tid, Lm, sm.qkm);
     __syncthreads();
 
     // ---- T = (I - L)^-1 (fp32, in place), then T -> a4 rows 0-63 (bf16)
@@ -480,7 +275,7 @@ __global__ void __launch_bounds__(kThreads, 2) chunk_prefill_tc_kernel(
     }
     // S (TMEM) -> bf16 MN-major tile (row = dk, col = dv); S *= e^gamma_L in TMEM
     {
-      const float egl = sm.eg[kC - 1];
+      const float egl = sm.sc.eg[kC - 1];
 #pragma unroll
       for (int cg = 0; cg < 4; ++cg) {
         float s[32];
@@ -524,7 +319,7 @@ __global__ void __launch_bounds__(kThreads, 2) chunk_prefill_tc_kernel(
     // MMA 4 adds the intra-chunk term onto the inter-chunk output.
     if (tid >= 64) {
       const int i = tid - 64;
-      const float f = sm.eg[i] * sm.nq[i];
+      const float f = sm.sc.eg[i] * sm.sc.nq[i];
 #pragma unroll
       for (int cg = 0; cg < 4; ++cg) {
         float x[32];
@@ -536,8 +331,8 @@ __global__ void __launch_bounds__(kThreads, 2) chunk_prefill_tc_kernel(
     }
     if (tid < 64) {
       const int i = tid;
-      const float xs = sm.eg[i] * sm.nk[i];
-      const float bi = sm.bet[i];
+      const float xs = sm.sc.eg[i] * sm.sc.nk[i];
+      const float bi = sm.sc.bet[i];
 #pragma unroll
       for (int cg = 0; cg < 4; ++cg) {
         float x[32];
@@ -579,7 +374,7 @@ __global__ void __launch_bounds__(kThreads, 2) chunk_prefill_tc_kernel(
     // ---- epilogue: W = nk e^(gamma_L-gamma) v' (rows 0-63); out (rows 64-127)
     if (tid < 64) {
       const int i = tid;
-      const float w = sm.nk[i] * expf(sm.gam[kC - 1] - sm.gam[i]);
+      const float w = sm.sc.nk[i] * expf(sm.sc.gam[kC - 1] - sm.sc.gam[i]);
 #pragma unroll
       for (int cg = 0; cg < 4; ++cg) {
         float vp[32];
@@ -627,6 +422,7 @@ __global__ void __launch_bounds__(kThreads, 2) chunk_prefill_tc_kernel(
     }
   }
   if (!ok && tid == 0) {   // drain loads still in flight before the CTA exits (bounded)
+#pragma unroll
     for (int i = 0; i < 3; ++i) mbar_wait(smem_u32(&sm.lbar[i]), lphase[i], kSpin);
   }
 
@@ -656,21 +452,6 @@ bool chunk_tc_supported(int D, const void* q, int64_t qs, const void* k, int64_t
          aligned16(pool) && qs % 8 == 0 && ks % 8 == 0 && vs % 8 == 0 && slot_stride % 4 == 0;
 }
 
-// bf16 [rows, cols] view with a row stride (elements), 64 x 64 boxes, 128B swizzle.
-static bool make_tile_map(CUtensorMap* m, const void* base, int64_t cols, int64_t rows,
-                          int64_t row_stride) {
-  EncodeTiledFn fn = encode_tiled();
-  if (fn == nullptr) return false;
-  const cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
-  const cuuint64_t strides[1] = {(cuuint64_t)row_stride * 2};
-  const cuuint32_t box[2] = {64, 64};
-  const cuuint32_t estr[2] = {1, 1};
-  return fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box,
-            estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) ==
-         CUDA_SUCCESS;
-}
-
 int chunk_prefill_tc(int n_seqs, int HV, cudaStream_t s, const bf16* q, int64_t qs,
                      const bf16* k, int64_t ks, const bf16* v, int64_t vs, const float* g,
                      const bf16* beta, float* pool, int64_t slot_stride, int64_t num_slots,
@@ -678,9 +459,9 @@ int chunk_prefill_tc(int n_seqs, int HV, cudaStream_t s, const bf16* q, int64_t 
                      bf16* out, int HK, float scale, const bf16* z, int64_t zs, const bf16* nw,
                      float eps, int32_t* status) {
   CUtensorMap tm_q, tm_k, tm_v;
-  if (!make_tile_map(&tm_q, q, (int64_t)HK * tc::kD, n_tokens, qs) ||
-      !make_tile_map(&tm_k, k, (int64_t)HK * tc::kD, n_tokens, ks) ||
-      !make_tile_map(&tm_v, v, (int64_t)HV * tc::kD, n_tokens, vs)) {
+  if (!tc::make_tile_map(&tm_q, q, (int64_t)HK * tc::kD, n_tokens, qs) ||
+      !tc::make_tile_map(&tm_k, k, (int64_t)HK * tc::kD, n_tokens, ks) ||
+      !tc::make_tile_map(&tm_v, v, (int64_t)HV * tc::kD, n_tokens, vs)) {
     set_error("gdn_chunk_prefill_varlen: cuTensorMapEncodeTiled failed");
     return GDN_ERR_CUDA;
   }

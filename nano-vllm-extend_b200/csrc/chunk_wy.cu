@@ -1,0 +1,669 @@
+// (c) Chunked gated-delta-rule prefill, split form (sm_100a): the
+// state-independent work of every chunk runs first, fully parallel, and the
+// serial chain per (sequence, v-head) keeps only the state-dependent steps.
+//
+//   chunk_index_kernel  chunk_start[r] = sum over earlier sequences of
+//                       ceil(len / 64) (the workspace's block numbering)
+//   chunk_prep_kernel   one CTA (128 threads, four per SM) per (chunk, v-head):
+//                       P = [K;Q][K;Q]^T on the tensor core, the l2 norms, the
+//                       decays, L and QKm, T = (I - L)^-1 (fp32), M2 = QKm T;
+//                       writes one 17,664-byte block: the [T; M2] tile as the
+//                       128B-swizzled shared-memory image MMA 4 reads, and the
+//                       per-token factors the chain applies
+//   chunk_chain_kernel  one CTA (256 threads, two per SM) per chain, longest
+//                       first; the fp32 state in TMEM; per chunk three M = 128
+//                       MMAs (XQ = [K;Q] S, [v'; out] += [T;M2] [R_hi;R_lo],
+//                       S += K^T [W_hi;W_lo]) and the CUDA-core phases between
+//                       them, split over 8 warps (warp w: TMEM lanes of quarter
+//                       w % 4, columns of half w / 4)
+//
+// The arithmetic is the single-kernel form's (chunk_tc.cu) step for step —
+// same operands, same roundings — so both give the same bits; the split only
+// changes where each step runs.  Blocks move by bulk copies (one store per
+// prep CTA, one load per chain chunk).  Every wait is bounded (status bit, TMEM freed, return).
+#include "chunk_common.cuh"
+
+namespace gdn {
+namespace tc {
+namespace wy {
+
+constexpr uint32_t kSpin = 1u << 22;
+constexpr uint32_t kTile = 16384;                  // [T; M2]: 128 rows x 128 B
+constexpr uint32_t kScal = 5 * kC * 4;             // xs, beta, fq, wk, (e^gamma_L, 0 ...)
+constexpr uint32_t kBlockBytes = kTile + kScal;    // 17,664 (a multiple of 128)
+constexpr int kPrepThreads = 128;
+constexpr int kChainThreads = 256;
+constexpr int kIndexThreads = 1024;
+
+// The chain's 128-row MMA operands interleave their two 64-row halves by 32
+// rows: tile rows [first 0-31; second 0-31; first 32-63; second 32-63] for
+// [K;Q] and [T;M2].  An MMA output row lands in the TMEM lane of its operand
+// row, and warp w (issuing on SM sub-partition w % 4) reaches lanes of
+// quarter w % 4 only, so each sub-partition then holds one quarter of the
+// heavy rows (R, W: the first half) and one of the light ones (QS, out).
+__host__ __device__ constexpr int ilv_row(int token, bool second) {
+  return token + (token & 32) + (second ? 32 : 0);
+}
+
+// ---------------------------------------------------------------- index
+// chunk_start[r] = first block of sequence r; chunk_info[b] = {first token row,
+// valid rows} of block b (valid rows 0 for the unused tail up to the capacity).
+// Sequences that are malformed (negative start or length, past n_tokens) get
+// no chunks (the chain kernel flags them); a sequence whose chunks would pass
+// the workspace's capacity (only overlapping, malformed cu_seqlens) is cut
+// short here and flagged by the chain kernel when its count does not match.
+__global__ void __launch_bounds__(kIndexThreads) chunk_index_kernel(
+    const int32_t* __restrict__ cu, int n_seqs, int64_t n_tokens, int max_seqlen, int64_t cap,
+    int32_t* __restrict__ chunk_start, int2* __restrict__ chunk_info) {
+  __shared__ long long wsum[32];
+  __shared__ long long carry;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  if (tid == 0) carry = 0;
+  __syncthreads();
+  for (int base = 0; base < n_seqs; base += kIndexThreads) {
+    const int i = base + tid;
+    long long n = 0, s = 0, l = 0;
+    if (i < n_seqs) {
+      s = cu[i];
+      l = (long long)cu[i + 1] - s;
+      if (s >= 0 && l > 0 && s + l <= n_tokens) {
+        l = min(l, (long long)max_seqlen);
+        n = (l + kC - 1) / kC;
+      }
+    }
+    long long x = n;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const long long y = __shfl_up_sync(0xffffffffu, x, o);
+      if (lane >= o) x += y;
+    }
+    if (lane == 31) wsum[warp] = x;
+    __syncthreads();
+    if (warp == 0) {
+      long long w = wsum[lane];
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const long long y = __shfl_up_sync(0xffffffffu, w, o);
+        if (lane >= o) w += y;
+      }
+      wsum[lane] = w;
+    }
+    __syncthreads();
+    const long long excl = carry + (warp > 0 ? wsum[warp - 1] : 0) + x - n;
+    if (i < n_seqs) {
+      chunk_start[i] = (int32_t)min(excl, (long long)cap);
+      for (long long c = 0; c < n && excl + c < cap; ++c)
+        chunk_info[excl + c] = make_int2((int)(s + c * kC), (int)min((long long)kC, l - c * kC));
+    }
+    __syncthreads();
+    if (tid == 0) carry += wsum[31];
+    __syncthreads();
+  }
+  const long long total = min(carry, (long long)cap);
+  if (tid == 0) chunk_start[n_seqs] = (int32_t)total;
+  for (long long b = total + tid; b < cap; b += kIndexThreads) chunk_info[b] = make_int2(0, 0);
+}
+
+// ---------------------------------------------------------------- prep
+struct __align__(1024) PrepSmem {
+  uint8_t kq[2][128 * 128];   // [K;Q]; after MMA 1: L / T (fp32), X, the QKm tile
+  uint8_t a4[128 * 128];      // [T ; M2] (interleaved rows) } one block image,
+  float f[5][kC];             // the factors               } stored by one bulk copy
+  ChunkScalars sc;
+  unsigned long long mbar, lbar;
+  uint32_t tmem_base;
+  int abort;
+};
+constexpr uint32_t kXOff = kC * kLP * 4;          // X after L / T (17,408 B)
+constexpr uint32_t kQkmOff = 21504;               // QKm tile (1024-aligned) after X
+
+__global__ void __launch_bounds__(kPrepThreads, 4) chunk_prep_kernel(
+    const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+    const float* __restrict__ g, const bf16* __restrict__ beta,
+    const int2* __restrict__ chunk_info, int HK, int HV, float scale,
+    uint8_t* __restrict__ blocks, int32_t* status) {
+  extern __shared__ uint8_t smem_raw[];
+  PrepSmem& sm = *reinterpret_cast<PrepSmem*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int b = blockIdx.x / HV;
+  const int h = blockIdx.x - b * HV;
+  const int hk = h / (HV / HK);
+  const int2 info = chunk_info[b];
+  const int64_t t0 = info.x;
+  const int nv = info.y;
+  if (nv <= 0) return;                   // past the last chunk
+
+  const uint32_t kq0 = smem_u32(sm.kq[0]);
+  const uint32_t bar = smem_u32(&sm.mbar), lbar = smem_u32(&sm.lbar);
+  if (tid == 0) {
+    mbar_init(bar, 1);
+    mbar_init(lbar, 1);
+    mbar_init_fence();
+    sm.abort = 0;
+    mbar_expect_tx(lbar, 4 * 8192);
+    for (int blk = 0; blk < 2; ++blk) {
+      tma_load_2d(kq0 + blk * 16384, &tm_k, hk * kD + blk * 64, (int)t0, lbar);
+      tma_load_2d(kq0 + blk * 16384 + 64 * 128, &tm_q, hk * kD + blk * 64, (int)t0, lbar);
+    }
+  }
+  if (tid < kC) {
+    float gv = 0.f, bv = 0.f;
+    if (tid < nv) {
+      gv = __ldg(g + (t0 + tid) * HV + h);
+      bv = __bfloat162float(beta[(t0 + tid) * HV + h]);
+    }
+    sm.sc.gam[tid] = gv;
+    sm.sc.bet[tid] = bv;
+  }
+  if (warp == 0) tmem_alloc(smem_u32(&sm.tmem_base), 128);
+  fence_before();
+  __syncthreads();
+  fence_after();
+  const uint32_t tbase = sm.tmem_base;
+  const uint32_t tl = tbase + ((uint32_t)(warp * 32) << 16);
+  // one thread waits on each barrier; the others wait at the CTA barrier
+  auto wait1 = [&](uint32_t mb, uint32_t ph) -> bool {
+    if (tid == 0 && !mbar_wait(mb, ph, kSpin)) {
+      sm.abort = 1;
+      if (status) atomicOr(status, GDN_STATUS_TIMEOUT);
+    }
+    __syncthreads();
+    fence_after();
+    return sm.abort == 0;
+  };
+  bool ok = wait1(lbar, 0);
+  if (ok) {
+    if (nv < kC) {   // rows past the sequence end: zero K and Q
+      for (int idx = tid; idx < (kC - nv) * 16; idx += kPrepThreads) {
+        const int i = nv + idx / 16, ch = idx % 16, blk = ch >> 3, c8 = (ch & 7) * 8;
+        const uint4 z = make_uint4(0, 0, 0, 0);
+        *reinterpret_cast<uint4*>(sm.kq[blk] + sw128(i, c8)) = z;
+        *reinterpret_cast<uint4*>(sm.kq[blk] + sw128(64 + i, c8)) = z;
+      }
+    }
+    if (warp == 0) decay_scan(sm.sc, lane);
+    fence_async_smem();
+    fence_before();
+    __syncthreads();
+    fence_after();
+    // (1) P = [K;Q] [K;Q]^T : M = 128, N = 128, K = 128
+    if (tid == 0) {
+#pragma unroll
+      for (int s = 0; s < 8; ++s) {
+        const uint32_t off = (uint32_t)(s >> 2) * 16384u + (uint32_t)(s & 3) * 32u;
+        mma_bf16(tbase, smem_desc(kq0 + off, 16, 1024), smem_desc(kq0 + off, 16, 1024),
+                 idesc_bf16(128, 128, false, false), s > 0);
+      }
+      mma_commit(bar);
+    }
+    ok = wait1(bar, 0);
+  }
+  if (ok) {
+    norms_from_diag(sm.sc, tl, 0, tid, scale);
+    __syncthreads();
+    uint8_t* const kqb = &sm.kq[0][0];                           // K / Q are consumed
+    float (*Lm)[kLP] = reinterpret_cast<float (*)[kLP]>(kqb);
+    float* Xs = reinterpret_cast<float*>(kqb + kXOff);
+    uint8_t* qkm = kqb + kQkmOff;
+    build_l_qkm(sm.sc, tl, 0, tid, Lm, qkm);
+    __syncthreads();
+    invert_unit_lower(Lm, Xs, tid);
+    for (int idx = tid; idx < kC * 8; idx += kPrepThreads) {
+      const int i = idx >> 3, c8 = (idx & 7) * 8;
+      st8(sm.a4, ilv_row(i, false), c8, &Lm[i][c8]);
+    }
+    fence_async_smem();
+    fence_before();
+    __syncthreads();
+    fence_after();
+    // (2) M2 = [QKm; *] T : M = 128 (rows 64-127 unused), N = 64, K = 64
+    if (tid == 0) {
+      const uint32_t qkm0 = kq0 + kQkmOff, a40 = smem_u32(sm.a4);
+#pragma unroll
+      for (int s = 0; s < 4; ++s)
+        mma_bf16(tbase, smem_desc(qkm0 + s * 32, 16, 1024),
+                 smem_desc(a40 + ilv_row(16 * s, false) * 128, 8192, 1024),
+                 idesc_bf16(128, 64, false, true), s > 0);
+      mma_commit(bar);
+    }
+    if (tid < kC) {   // per-token factors of the chain's phases
+      const ChunkScalars& s = sm.sc;
+      sm.f[0][tid] = s.eg[tid] * s.nk[tid];                             // R: e^gamma nk
+      sm.f[1][tid] = s.bet[tid];                                        // R: beta
+      sm.f[2][tid] = s.eg[tid] * s.nq[tid];                             // QS: e^gamma nq
+      sm.f[3][tid] = s.nk[tid] * expf(s.gam[kC - 1] - s.gam[tid]);      // W: nk e^(gL - g)
+      sm.f[4][tid] = tid == 0 ? s.eg[kC - 1] : 0.f;                     // S: e^gamma_L
+    }
+    ok = wait1(bar, 1);
+    if (ok) {
+      if (tid < 64) {   // M2 rows -> the a4 rows of the second half
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh) {
+          float m[32];
+          tmem_ld32(tl + hh * 32, m);
+#pragma unroll
+          for (int q8 = 0; q8 < 4; ++q8)
+            st8(sm.a4, ilv_row(tid, true), hh * 32 + q8 * 8, m + q8 * 8);
+        }
+      }
+      fence_async_smem();
+      __syncthreads();
+      if (tid == 0) {
+        bulk_store(blocks + ((int64_t)b * HV + h) * kBlockBytes, smem_u32(sm.a4), kBlockBytes);
+        bulk_wait_read();
+      }
+    }
+  }
+  fence_before();
+  __syncthreads();
+  fence_after();
+  if (warp == 0) tmem_dealloc(tbase, 128);
+}
+
+// ---------------------------------------------------------------- chain
+struct __align__(1024) ChainSmem {
+  uint8_t kq[2][128 * 128];   // [dk block][row][128 B]: K / Q rows interleaved (ilv_row)
+  uint8_t scratch[32768];     // the bf16 S tile for MMA 3, then R, then W (hi / lo)
+  uint8_t a4[128 * 128];      // [T ; M2] from the chunk's block
+  uint8_t v[2][64 * 128];     // [dv block][token row][128 B]
+  float f[5][kC];             // the block's per-token factors
+  unsigned long long mbar;    // MMA completion
+  unsigned long long lbar[4]; // loads: K, Q, V, block
+  uint32_t tmem_base;
+  int abort;
+};
+
+__global__ void __launch_bounds__(kChainThreads, 2) chunk_chain_kernel(
+    const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+    const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_out,
+    const uint8_t* __restrict__ blocks,
+    const int32_t* __restrict__ chunk_start, float* __restrict__ pool, int64_t slot_stride,
+    int64_t num_slots, const int64_t* __restrict__ ids, const int32_t* __restrict__ cu,
+    int64_t n_tokens, int max_seqlen, bf16* __restrict__ out, int HK, int HV, int32_t* status) {
+  extern __shared__ uint8_t smem_raw[];
+  ChainSmem& sm = *reinterpret_cast<ChainSmem*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int qd = warp & 3, half = warp >> 2;
+  const int row = qd * 32 + lane;        // TMEM lane: dk row of S, or row of a 128-row tile
+  const bool second = qd & 1;            // interleaved tile row of the second half (Q / M2)
+  const int rank = blockIdx.x / HV;
+  const int h = blockIdx.x - rank * HV;
+  const int hk = h / (HV / HK);
+  const int n_seqs = gridDim.x / HV;
+  const int r = lpt_sequence<kChainThreads>(cu, n_seqs, rank, tid);
+
+  const int64_t slot = ids[r];
+  if (!slot_ok(slot, num_slots, status)) return;
+  const int64_t start = cu[r];
+  int64_t len = (int64_t)cu[r + 1] - start;
+  if (start < 0 || len < 0 || start + len > n_tokens) {
+    if (tid == 0 && status) atomicOr(status, GDN_STATUS_BAD_SEQLEN);
+    return;
+  }
+  if (len > max_seqlen) {
+    if (tid == 0 && status) atomicOr(status, GDN_STATUS_BAD_SEQLEN);
+    len = max_seqlen;
+  }
+  if (len == 0) return;
+  const int nchunks = (int)((len + kC - 1) / kC);
+  const int cs = chunk_start[r];
+  if (chunk_start[r + 1] - cs != nchunks) {   // cut short by the index (overlapping cu)
+    if (tid == 0 && status) atomicOr(status, GDN_STATUS_BAD_SEQLEN);
+    return;
+  }
+
+  const uint32_t kq0 = smem_u32(sm.kq[0]);
+  // K / Q rows in 32-row boxes at their interleaved tile rows
+  auto load_k = [&](int c) {
+    const uint32_t b = smem_u32(&sm.lbar[0]);
+    mbar_expect_tx(b, 2 * 8192);
+    for (int blk = 0; blk < 2; ++blk)
+      for (int hf = 0; hf < 2; ++hf)
+        tma_load_2d(kq0 + blk * 16384 + ilv_row(32 * hf, false) * 128, &tm_k, hk * kD + blk * 64,
+                    (int)(start + c * kC + 32 * hf), b);
+  };
+  auto load_q = [&](int c) {
+    const uint32_t b = smem_u32(&sm.lbar[1]);
+    mbar_expect_tx(b, 2 * 8192);
+    for (int blk = 0; blk < 2; ++blk)
+      for (int hf = 0; hf < 2; ++hf)
+        tma_load_2d(kq0 + blk * 16384 + ilv_row(32 * hf, true) * 128, &tm_q, hk * kD + blk * 64,
+                    (int)(start + c * kC + 32 * hf), b);
+  };
+  auto load_v = [&](int c) {
+    const uint32_t b = smem_u32(&sm.lbar[2]);
+    mbar_expect_tx(b, 2 * 8192);
+    for (int blk = 0; blk < 2; ++blk)
+      tma_load_2d(smem_u32(sm.v[blk]), &tm_v, h * kD + blk * 64, (int)(start + c * kC), b);
+  };
+  auto load_blk = [&](int c) {
+    const uint32_t b = smem_u32(&sm.lbar[3]);
+    const uint8_t* src = blocks + ((int64_t)(cs + c) * HV + h) * kBlockBytes;
+    mbar_expect_tx(b, kBlockBytes);
+    bulk_load(smem_u32(sm.a4), src, kTile, b);
+    bulk_load(smem_u32(&sm.f[0][0]), src + kTile, kScal, b);
+  };
+
+  const uint32_t bar = smem_u32(&sm.mbar);
+  if (tid == 0) {
+    mbar_init(bar, 1);
+    for (int i = 0; i < 4; ++i) mbar_init(smem_u32(&sm.lbar[i]), 1);
+    mbar_init_fence();
+    sm.abort = 0;
+  }
+  __syncthreads();
+  if (tid == 0) {
+    load_blk(0);
+    load_k(0);
+    load_q(0);
+    load_v(0);
+  }
+  uint32_t lphase[4] = {0u, 0u, 0u, 0u};
+  if (warp == 0) tmem_alloc(smem_u32(&sm.tmem_base), 256);
+  fence_before();
+  __syncthreads();
+  fence_after();
+  const uint32_t tbase = sm.tmem_base;
+  const uint32_t tl = tbase + ((uint32_t)(qd * 32) << 16);   // this warp's lane window
+  constexpr uint32_t kColS = 0, kColW = 128;
+  const uint32_t c0 = (uint32_t)half * 64;                  // this warp's column half
+  uint32_t phase = 0;
+
+  // One thread waits on each barrier; the others wait at the CTA barrier
+  // that follows (no issue slots spent polling).
+  auto wait_mma = [&]() -> bool {
+    if (tid == 0 && !mbar_wait(bar, phase, kSpin)) {
+      sm.abort = 1;
+      if (status) atomicOr(status, GDN_STATUS_TIMEOUT);
+    }
+    phase ^= 1u;
+    __syncthreads();
+    fence_after();
+    return sm.abort == 0;
+  };
+  auto wait_load = [&](int i) {     // thread 0 only; a CTA barrier must follow
+    if (!mbar_wait(smem_u32(&sm.lbar[i]), lphase[i], kSpin)) {
+      sm.abort = 1;
+      if (status) atomicOr(status, GDN_STATUS_TIMEOUT);
+    }
+    lphase[i] ^= 1u;
+  };
+  auto sync_for_mma = [&]() {
+    fence_async_smem();
+    fence_before();
+    __syncthreads();
+    fence_after();
+  };
+
+  // initial state -> TMEM (thread: dk row `row`, dv columns [c0, c0 + 64))
+  float* sp = pool + slot * slot_stride + (int64_t)h * kD * kD + (int64_t)row * kD + c0;
+#pragma unroll
+  for (int cg = 0; cg < 2; ++cg) {
+    float s[32];
+    const float4* src = reinterpret_cast<const float4*>(sp + cg * 32);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float4 x = src[i];
+      s[4 * i] = x.x; s[4 * i + 1] = x.y; s[4 * i + 2] = x.z; s[4 * i + 3] = x.w;
+    }
+    tmem_st32(tl + kColS + c0 + cg * 32, s);
+  }
+  tmem_wait_st();
+
+  const uint32_t scr0 = smem_u32(sm.scratch);
+  const uint32_t a40 = smem_u32(sm.a4);
+  constexpr uint32_t kLoOff = 16384;                 // R / W lo tiles after the hi tiles
+  uint8_t* whi = sm.scratch + half * 8192;           // this warp's dv block of R / W
+  uint8_t* wlo = whi + kLoOff;
+  bool ok = true;
+
+  for (int c = 0; c < nchunks && ok; ++c) {
+    const int64_t t0 = start + (int64_t)c * kC;
+    const int nv = (int)min((int64_t)kC, len - (int64_t)c * kC);
+    const bool full = nv == kC;
+    if (tid == 0) wait_load(3);
+    __syncthreads();
+    if (sm.abort) { ok = false; break; }
+    const int i = (qd >> 1) * 32 + lane;            // token of this thread's tile row
+    const float f0 = sm.f[second ? 2 : 0][i];       // e^gamma nk (R rows) | e^gamma nq (QS rows)
+    const float bi = sm.f[1][i];
+    const float wk = sm.f[3][i];
+    const float egl = sm.f[4][0];
+
+    // S (state after the previous chunk) -> bf16 MN-major tile (row = dk,
+    // col = dv) for MMA 3; then S *= e^gamma_L in TMEM for MMA 5
+    {
+      float s[2][32];
+      tmem_ld32x2(tl + kColS + c0, tl + kColS + c0 + 32, s[0], s[1]);
+#pragma unroll
+      for (int cg = 0; cg < 2; ++cg) {
+#pragma unroll
+        for (int q8 = 0; q8 < 4; ++q8)
+          st8(sm.scratch + half * 16384, row, cg * 32 + q8 * 8, s[cg] + q8 * 8);
+#pragma unroll
+        for (int e = 0; e < 32; e += 2)
+          fmul2(s[cg][e], s[cg][e + 1], s[cg][e], s[cg][e + 1], egl, egl);
+        tmem_st32(tl + kColS + c0 + cg * 32, s[cg]);
+      }
+    }
+    tmem_wait_st();
+    if (tid == 0) {
+      wait_load(0);
+      wait_load(1);
+    }
+    if (nv < kC) {   // clear rows past the sequence end in the K and Q tiles
+      __syncthreads();
+      for (int idx = tid; idx < (kC - nv) * 16; idx += kChainThreads) {
+        const int ii = nv + idx / 16, ch = idx % 16, blk = ch >> 3, c8 = (ch & 7) * 8;
+        const uint4 z = make_uint4(0, 0, 0, 0);
+        *reinterpret_cast<uint4*>(sm.kq[blk] + sw128(ilv_row(ii, false), c8)) = z;
+        *reinterpret_cast<uint4*>(sm.kq[blk] + sw128(ilv_row(ii, true), c8)) = z;
+      }
+    }
+    sync_for_mma();
+    if (sm.abort) { ok = false; break; }
+
+    // ---- (3) XQ = [K; Q] S : M=128, N=128, K=128 (dk); B = S rows (MN-major)
+    if (tid == 0) {
+#pragma unroll
+      for (int s = 0; s < 8; ++s)
+        mma_bf16(tbase + kColW,
+                 smem_desc(kq0 + (uint32_t)(s >> 2) * 16384u + (uint32_t)(s & 3) * 32u, 16, 1024),
+                 smem_desc(scr0 + s * 2048, 16384, 1024), idesc_bf16(128, 128, false, true), s > 0);
+      mma_commit(bar);
+    }
+    if (tid == 0) wait_load(2);                        // V, before the barrier in wait_mma
+    if (!(ok = wait_mma())) break;
+    if (tid == 0 && c + 1 < nchunks) load_q(c + 1);   // Q rows are no longer read this chunk
+
+    // ---- R = beta (v - e^gamma nk X) -> hi / lo tiles (K rows), those TMEM rows cleared;
+    // Q rows: QS *= e^gamma nq in TMEM (fp32)
+    if (second) {
+      float x[2][32];
+      tmem_ld32x2(tl + kColW + c0, tl + kColW + c0 + 32, x[0], x[1]);
+#pragma unroll
+      for (int cg = 0; cg < 2; ++cg) {
+#pragma unroll
+        for (int e = 0; e < 32; e += 2)
+          fmul2(x[cg][e], x[cg][e + 1], x[cg][e], x[cg][e + 1], f0, f0);
+        tmem_st32(tl + kColW + c0 + cg * 32, x[cg]);
+      }
+    } else {
+      float xx[2][32];
+      tmem_ld32x2(tl + kColW + c0, tl + kColW + c0 + 32, xx[0], xx[1]);
+#pragma unroll
+      for (int cg = 0; cg < 2; ++cg) {
+        float (&x)[32] = xx[cg];
+#pragma unroll
+        for (int q8 = 0; q8 < 4; ++q8) {
+          float vv[8], rr[8];
+          const int chk = cg * 4 + q8;               // 16-byte chunk within the dv block
+          unpack8(i < nv ? *reinterpret_cast<const uint4*>(sm.v[half] + sw128(i, chk * 8))
+                         : make_uint4(0, 0, 0, 0), vv);
+#pragma unroll
+          for (int e = 0; e < 8; e += 2) {
+            ffma2(rr[e], rr[e + 1], -f0, -f0, x[q8 * 8 + e], x[q8 * 8 + e + 1], vv[e], vv[e + 1]);
+            fmul2(rr[e], rr[e + 1], rr[e], rr[e + 1], bi, bi);
+          }
+          split8(rr, whi, wlo, sw128(i, chk * 8));
+        }
+#pragma unroll
+        for (int e = 0; e < 32; ++e) x[e] = 0.f;
+        tmem_st32(tl + kColW + c0 + cg * 32, x);
+      }
+    }
+    tmem_wait_st();
+    sync_for_mma();
+
+    // ---- (4) W-region += [T;M2] [R_hi;R_lo] : T rows -> v', M2 rows -> out
+    if (tid == 0) {
+#pragma unroll
+      for (int s = 0; s < 8; ++s)
+        mma_bf16(tbase + kColW, smem_desc(a40 + (s & 3) * 32, 16, 1024),
+                 smem_desc((s < 4 ? scr0 : scr0 + kLoOff) + (s & 3) * 2048, 8192, 1024),
+                 idesc_bf16(128, 128, false, true), 1u);
+      mma_commit(bar);
+    }
+    if (!(ok = wait_mma())) break;
+    if (tid == 0 && c + 1 < nchunks) load_blk(c + 1);   // a4 and the factors are consumed
+
+    // ---- epilogue: W = nk e^(gamma_L-gamma) v' (T rows); out (M2 rows) -> bf16
+    // tile in the (consumed) v buffer, stored by TMA while MMA 5 runs
+    {
+      float vv[2][32];
+      tmem_ld32x2(tl + kColW + c0, tl + kColW + c0 + 32, vv[0], vv[1]);
+      if (!second) {
+#pragma unroll
+        for (int cg = 0; cg < 2; ++cg) {
+#pragma unroll
+          for (int q8 = 0; q8 < 4; ++q8) {
+            float x[8];
+#pragma unroll
+            for (int e = 0; e < 8; e += 2)
+              fmul2(x[e], x[e + 1], wk, wk, vv[cg][q8 * 8 + e], vv[cg][q8 * 8 + e + 1]);
+            split8(x, whi, wlo, sw128(i, cg * 32 + q8 * 8));
+          }
+        }
+      } else if (full || i < nv) {
+#pragma unroll
+        for (int cg = 0; cg < 2; ++cg)
+#pragma unroll
+          for (int q8 = 0; q8 < 4; ++q8) {
+            if (full) {
+              st8(sm.v[half], i, cg * 32 + q8 * 8, vv[cg] + q8 * 8);
+            } else {   // a partial last chunk: rows past the end belong to the next sequence
+              *reinterpret_cast<uint4*>(out + ((t0 + i) * HV + h) * kD + c0 + cg * 32 + q8 * 8) =
+                  pack8(vv[cg] + q8 * 8);
+            }
+          }
+      }
+    }
+    sync_for_mma();
+
+    // ---- (5) S += K^T [W_hi;W_lo] : M=128 (dk), N=128, K=64+64; A = K^T (MN-major)
+    if (tid == 0) {
+#pragma unroll
+      for (int s = 0; s < 8; ++s)
+        mma_bf16(tbase + kColS, smem_desc(kq0 + ilv_row(16 * (s & 3), false) * 128, 16384, 1024),
+                 smem_desc((s < 4 ? scr0 : scr0 + kLoOff) + (s & 3) * 2048, 8192, 1024),
+                 idesc_bf16(128, 128, true, true), 1u);
+      mma_commit(bar);
+      if (full) {
+        for (int blk = 0; blk < 2; ++blk)
+          tma_store_2d(&tm_out, h * kD + blk * 64, (int)t0, smem_u32(sm.v[blk]));
+        bulk_commit();
+      }
+    }
+    if (!(ok = wait_mma())) break;
+    if (tid == 0 && c + 1 < nchunks) {
+      load_k(c + 1);                                  // the K rows are free
+      bulk_wait_read();                               // the out tile has left the v buffer
+      load_v(c + 1);
+    }
+  }
+  if (!ok && tid == 0) {   // drain loads still in flight before the CTA exits (bounded)
+#pragma unroll
+    for (int i = 0; i < 4; ++i) mbar_wait(smem_u32(&sm.lbar[i]), lphase[i], kSpin);
+  }
+  if (tid == 0) bulk_wait_all();   // out tiles written before the CTA leaves
+  if (ok) {   // final state -> pool slot
+#pragma unroll
+    for (int cg = 0; cg < 2; ++cg) {
+      float s[32];
+      tmem_ld32(tl + kColS + c0 + cg * 32, s);
+      float4* dst = reinterpret_cast<float4*>(sp + cg * 32);
+#pragma unroll
+      for (int q = 0; q < 8; ++q)
+        dst[q] = make_float4(s[4 * q], s[4 * q + 1], s[4 * q + 2], s[4 * q + 3]);
+    }
+  }
+  fence_before();
+  __syncthreads();
+  fence_after();
+  if (warp == 0) tmem_dealloc(tbase, 256);
+}
+
+}  // namespace wy
+}  // namespace tc
+
+int64_t chunk_wy_capacity(int64_t n_tokens, int64_t n_seqs) {
+  return (n_tokens + (tc::kC - 1) * n_seqs) / tc::kC;
+}
+
+// Workspace: chunk_start (int32 x n_seqs + 1) | chunk_info (int2 x capacity) |
+// blocks (capacity x HV x 17,664 B), each part 256-byte aligned.
+static int64_t align256(int64_t x) { return (x + 255) / 256 * 256; }
+
+int64_t chunk_wy_workspace_bytes(int64_t n_tokens, int64_t n_seqs, int64_t HV) {
+  const int64_t cap = chunk_wy_capacity(n_tokens, n_seqs);
+  return align256((n_seqs + 1) * 4) + align256(cap * 8) + cap * HV * tc::wy::kBlockBytes;
+}
+
+int chunk_prefill_wy(int n_seqs, int HV, cudaStream_t s, const bf16* q, int64_t qs,
+                     const bf16* k, int64_t ks, const bf16* v, int64_t vs, const float* g,
+                     const bf16* beta, float* pool, int64_t slot_stride, int64_t num_slots,
+                     const int64_t* ids, const int32_t* cu, int64_t n_tokens, int max_seqlen,
+                     bf16* out, int HK, float scale, void* workspace, int32_t* status) {
+  using namespace tc;
+  CUtensorMap tm_q, tm_k, tm_v, tm_q32, tm_k32, tm_out;
+  if (!make_tile_map(&tm_q, q, (int64_t)HK * kD, n_tokens, qs) ||
+      !make_tile_map(&tm_k, k, (int64_t)HK * kD, n_tokens, ks) ||
+      !make_tile_map(&tm_q32, q, (int64_t)HK * kD, n_tokens, qs, 32) ||
+      !make_tile_map(&tm_k32, k, (int64_t)HK * kD, n_tokens, ks, 32) ||
+      !make_tile_map(&tm_v, v, (int64_t)HV * kD, n_tokens, vs) ||
+      !make_tile_map(&tm_out, out, (int64_t)HV * kD, n_tokens, (int64_t)HV * kD)) {
+    set_error("gdn_chunk_prefill_varlen: cuTensorMapEncodeTiled failed");
+    return GDN_ERR_CUDA;
+  }
+  const int64_t cap = chunk_wy_capacity(n_tokens, n_seqs);
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  int32_t* chunk_start = reinterpret_cast<int32_t*>(ws);
+  int2* chunk_info = reinterpret_cast<int2*>(ws + align256((n_seqs + 1) * 4));
+  uint8_t* blocks = ws + align256((n_seqs + 1) * 4) + align256(cap * 8);
+  const size_t prep_smem = sizeof(wy::PrepSmem) + 1024;
+  const size_t chain_smem = sizeof(wy::ChainSmem) + 1024;
+  cudaError_t e = cudaFuncSetAttribute(wy::chunk_prep_kernel,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, (int)prep_smem);
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(wy::chunk_chain_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)chain_smem);
+  if (e != cudaSuccess) {
+    set_error("gdn_chunk_prefill_varlen: cudaFuncSetAttribute failed: %s", cudaGetErrorString(e));
+    return GDN_ERR_CUDA;
+  }
+  wy::chunk_index_kernel<<<1, wy::kIndexThreads, 0, s>>>(cu, n_seqs, n_tokens, max_seqlen, cap,
+                                                         chunk_start, chunk_info);
+  int rc = check_launch("gdn_chunk_prefill_varlen");
+  if (rc != GDN_OK || cap == 0) return rc;
+  wy::chunk_prep_kernel<<<(unsigned)(cap * HV), wy::kPrepThreads, prep_smem, s>>>(
+      tm_q, tm_k, g, beta, chunk_info, HK, HV, scale, blocks, status);
+  if ((rc = check_launch("gdn_chunk_prefill_varlen")) != GDN_OK) return rc;
+  wy::chunk_chain_kernel<<<(unsigned)((int64_t)n_seqs * HV), wy::kChainThreads, chain_smem, s>>>(
+      tm_q32, tm_k32, tm_v, tm_out, blocks, chunk_start, pool, slot_stride, num_slots, ids, cu, n_tokens,
+      max_seqlen, out, HK, HV, status);
+  return check_launch("gdn_chunk_prefill_varlen");
+}
+
+}  // namespace gdn

@@ -123,6 +123,33 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
   for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
 
+// Two 32-column loads (columns [a, a + 32) and [b, b + 32)) behind one wait.
+__device__ __forceinline__ void tmem_ld32x2(uint32_t ta, uint32_t tb, float (&va)[32],
+                                            float (&vb)[32]) {
+  uint32_t r[64];
+#define GDN_LD32(R, T)                                                                          \
+  asm volatile(                                                                                 \
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "                                                 \
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"                                 \
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"                \
+      : "=r"(R[0]), "=r"(R[1]), "=r"(R[2]), "=r"(R[3]), "=r"(R[4]), "=r"(R[5]), "=r"(R[6]),     \
+        "=r"(R[7]), "=r"(R[8]), "=r"(R[9]), "=r"(R[10]), "=r"(R[11]), "=r"(R[12]),              \
+        "=r"(R[13]), "=r"(R[14]), "=r"(R[15]), "=r"(R[16]), "=r"(R[17]), "=r"(R[18]),           \
+        "=r"(R[19]), "=r"(R[20]), "=r"(R[21]), "=r"(R[22]), "=r"(R[23]), "=r"(R[24]),           \
+        "=r"(R[25]), "=r"(R[26]), "=r"(R[27]), "=r"(R[28]), "=r"(R[29]), "=r"(R[30]),           \
+        "=r"(R[31])                                                                             \
+      : "r"(T))
+  GDN_LD32(r, ta);
+  GDN_LD32((r + 32), tb);
+#undef GDN_LD32
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 32; ++i) {
+    va[i] = __uint_as_float(r[i]);
+    vb[i] = __uint_as_float(r[32 + i]);
+  }
+}
+
 __device__ __forceinline__ void tmem_st32(uint32_t taddr, const float (&v)[32]) {
   asm volatile(
       "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
@@ -177,6 +204,22 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst_smem, const void* tmap,
       "l"(tmap), "r"(x), "r"(y), "r"(mbar)
       : "memory");
 }
+// TMA: 2-D tiled store shared -> global (the tensor map's box), tracked by the
+// issuing thread's bulk group.  Generic-proxy writes of the source must be
+// fenced (fence_async_smem) before the store is issued.
+__device__ __forceinline__ void tma_store_2d(const void* tmap, int x, int y, uint32_t src_smem) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];" ::"l"(tmap),
+      "r"(x), "r"(y), "r"(src_smem)
+      : "memory");
+}
+__device__ __forceinline__ void bulk_commit() {
+  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+// Wait until every bulk store of this thread is complete (global writes done).
+__device__ __forceinline__ void bulk_wait_all() {
+  asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+}
 // 1-D bulk copy global -> shared (16-byte aligned addresses, size a multiple of
 // 16), completing on an mbarrier (transaction bytes).  No cluster multicast.
 __device__ __forceinline__ void bulk_load(uint32_t dst_smem, const void* src, uint32_t bytes,
@@ -186,6 +229,19 @@ __device__ __forceinline__ void bulk_load(uint32_t dst_smem, const void* src, ui
           "r"(dst_smem),
       "l"(src), "r"(bytes), "r"(mbar)
       : "memory");
+}
+// 1-D bulk copy shared -> global (16-byte aligned addresses, size a multiple
+// of 16), tracked by the issuing thread's bulk group.  Generic-proxy writes of
+// the source must be fenced (fence_async_smem) before the copy is issued.
+__device__ __forceinline__ void bulk_store(void* dst, uint32_t src_smem, uint32_t bytes) {
+  asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(dst),
+               "r"(src_smem), "r"(bytes)
+               : "memory");
+  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+// Wait until every bulk store of this thread has finished reading shared memory.
+__device__ __forceinline__ void bulk_wait_read() {
+  asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
 }
 // Plain arrival (completes a phase of a count-1 barrier without a copy).
 __device__ __forceinline__ void mbar_arrive(uint32_t bar) {

@@ -274,15 +274,24 @@ def recurrent_gdn_inplace(q, k, v, g, beta, s_pool, ids, z=None, norm_weight=Non
     return out
 
 
+def chunk_prefill_workspace_bytes(n_tokens: int, n_seqs: int, HV: int, DK: int, DV: int) -> int:
+    """Device scratch the split chunk prefill needs (0: the shape has no split form)."""
+    return int(_lib.load().gdn_chunk_prefill_workspace_bytes(n_tokens, n_seqs, HV, DK, DV))
+
+
 def chunk_gated_delta_rule_varlen(q, k, v, g, beta, s_pool, ids, cu_seqlens,
                                   max_seqlen: int, z=None, norm_weight=None,
-                                  eps: float = 1e-6, out=None) -> torch.Tensor:
+                                  eps: float = 1e-6, out=None,
+                                  split: bool = True) -> torch.Tensor:
     """Varlen chunked prefill (the chunk rule of qwen3_5.py:140-227 driven by
     cu_seqlens as at :956-961), initial state read from and final state
     written to ``s_pool[ids[r]]``.  q/k [N, HK, DK], v [N, HV, DV] (row
-    views allowed), g fp32 / beta bf16 [N, HV].  Returns out [N, HV, DV];
-    with ``z`` / ``norm_weight`` the gated RMSNorm is fused as in
-    :func:`recurrent_gdn_inplace`."""
+    views allowed), g fp32 / beta bf16 [N, HV].  Returns out [N, HV, DV]; with ``z`` /
+    ``norm_weight`` the gated RMSNorm is fused as in
+    :func:`recurrent_gdn_inplace`.  ``split`` (head dim 128) runs the split
+    form with a workspace from torch's caching allocator, as the reference
+    allocates its chunk intermediates per call; False runs the one-kernel
+    form (same bits, no workspace)."""
     _cuda(q, k, v, g, beta, s_pool, ids, cu_seqlens)
     N, HK, DK, qs = _heads(q, "q")
     N_k, HK_k, DK_k, ks = _heads(k, "k")
@@ -298,11 +307,13 @@ def chunk_gated_delta_rule_varlen(q, k, v, g, beta, s_pool, ids, cu_seqlens,
     assert cu.numel() == ids.numel() + 1
     z3, zs, nw = _norm_args(z, norm_weight, N, HV, DV)
     out = _out_buffer(out, (N, HV, DV), v.device)
+    ws_bytes = chunk_prefill_workspace_bytes(N, ids.numel(), HV, DK, DV) if split else 0
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=v.device) if ws_bytes else None
     rc = _lib.load().gdn_chunk_prefill_varlen(
         _p(q), qs, _p(k), ks, _p(v), vs, _p(g), _p(beta), _p(s_pool), _slot_stride(s_pool),
         s_pool.shape[0], _p(ids), _p(cu), ids.numel(), N, int(max_seqlen), _p(out), HK, HV, DK,
-        DV, DK ** -0.5, _p(z3), zs, _p(nw), float(eps), _p(status_word(v.device)),
-        _stream_ptr(v.device))
+        DV, DK ** -0.5, _p(z3), zs, _p(nw), float(eps), _p(ws), ws_bytes,
+        _p(status_word(v.device)), _stream_ptr(v.device))
     _lib.check(rc, "gdn_chunk_prefill_varlen")
     return out
 

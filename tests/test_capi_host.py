@@ -78,8 +78,29 @@ def test_host_validation_errors(pkg):
     # chunk: unsupported dims
     rc, msg = _call(pkg, "gdn_chunk_prefill_varlen", None, 64, None, 64, None, 64, None, None,
                     None, 1 << 20, 2, None, None, 1, 1, 1, None, 1, 1, 32, 32, 0.1, None, 0, None,
-                    1e-6, None, None)
+                    1e-6, None, 0, None, None)
     assert rc == L.GDN_ERR_UNSUPPORTED
+
+
+def test_chunk_workspace_size_and_too_small_workspace(pkg):
+    """The split chunk prefill's scratch: one 17,664-byte block per (chunk, v-head) for up
+    to cap = (n_tokens + 63 n_seqs) / 64 chunks, after the int32 chunk starts and the
+    int2 per-chunk rows (each part 256-byte padded); none for head dim 64.  A workspace
+    below that size is rejected before any launch."""
+    L = pkg._lib
+    lib = L.load()
+    n, seqs, hv = 282505, 64, 32
+    cap = (n + 63 * seqs) // 64
+    a256 = lambda x: (x + 255) // 256 * 256
+    want = a256((seqs + 1) * 4) + a256(cap * 8) + cap * hv * 17664
+    assert lib.gdn_chunk_prefill_workspace_bytes(n, seqs, hv, 128, 128) == want
+    assert lib.gdn_chunk_prefill_workspace_bytes(n, seqs, hv, 64, 64) == 0
+    assert lib.gdn_chunk_prefill_workspace_bytes(0, seqs, hv, 128, 128) == 0
+    fake = 1 << 20                                   # aligned, never dereferenced
+    rc, msg = _call(pkg, "gdn_chunk_prefill_varlen", fake, 512, fake, 512, fake, 1024, fake,
+                    fake, fake, 8 * 128 * 128, 4, fake, fake, 2, 300, 200, fake, 4, 8, 128, 128,
+                    0.1, None, 0, None, 1e-6, fake, 1000, None, None)
+    assert rc == L.GDN_ERR_INVALID_ARGUMENT and "workspace" in msg
 
 
 def test_empty_calls_are_noops(pkg):

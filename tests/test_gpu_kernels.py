@@ -296,6 +296,59 @@ def test_chunk_split_equals_one_shot(ops):
     assert state_rel(host(p2), host(p1)) <= STATE_RTOL
 
 
+@pytest.mark.parametrize("lens,HK,HV", [
+    ([1, 2, 63, 64, 65, 130, 0, 200, 1000], 2, 4),    # ragged; two v-heads per k-head
+    ([300, 5], 4, 4),                                 # one v-head per k-head
+    ([129], 1, 4),                                    # four v-heads per k-head
+    (list(I.rng(33).integers(0, 150, 300)), 1, 2),    # > 256 sequences: launch-order chains
+])
+def test_chunk_split_form_equals_one_kernel_form(ops, lens, HK, HV):
+    """Head dim 128: the split form (per-chunk prep pass + chain) and the
+    one-kernel form compute the same steps with the same roundings, so the
+    outputs and the states agree bit for bit."""
+    D = 128
+    lens = [int(x) for x in lens]
+    N = sum(lens)
+    q, k, v, g, beta = I.core_inputs(N, HK, D, HV, D, seed=31 + len(lens))
+    q, k, v, beta = (O.round_bf16(t) for t in (q, k, v, beta))
+    slots = len(lens) + 2
+    pool = (I.rng(32).standard_normal((slots, HV, D, D)) * 0.02).astype(np.float32)
+    ids = I.rng(34).permutation(slots)[:len(lens)]
+    cu = I.cu_from_lens(lens)
+    res = []
+    for split in (True, False):
+        pool_d = f32(pool)
+        out = ops.chunk_gated_delta_rule_varlen(bf(q), bf(k), bf(v), f32(g), bf(beta), pool_d,
+                                                i64(ids), i32(cu), max(lens), split=split)
+        res.append((out, pool_d))
+    ops.check_status()
+    assert torch.equal(res[0][0], res[1][0])
+    assert torch.equal(res[0][1], res[1][1])
+
+
+def test_chunk_split_overlapping_cu_is_flagged(ops):
+    """Overlapping (malformed) cu_seqlens can ask for more chunks than the
+    workspace holds for n_tokens rows: the sequence cut short is flagged and
+    skipped (its slot untouched); the well-formed first sequence is exact."""
+    HK, HV, D, N = 1, 2, 128, 160
+    q, k, v, g, beta = I.core_inputs(N, HK, D, HV, D, seed=73)
+    q, k, v, beta = (O.round_bf16(t) for t in (q, k, v, beta))
+    pool = (I.rng(74).standard_normal((4, HV, D, D)) * 0.02).astype(np.float32)
+    pool_d = f32(pool)
+    ops.check_status()
+    # (0, 150): 3 chunks; (150, 10): negative length; (10, 160): 3 chunks > capacity 5
+    ops.chunk_gated_delta_rule_varlen(bf(q), bf(k), bf(v), f32(g), bf(beta), pool_d,
+                                      i64([0, 1, 2]), i32([0, 150, 10, 160]), 150)
+    with pytest.raises(ValueError):
+        ops.check_status()
+    got = host(pool_d)
+    assert np.array_equal(got[[1, 2, 3]], pool[[1, 2, 3]])
+    ref_pool = pool.copy()
+    O.chunk_prefill_varlen(q[:150], k[:150], v[:150], g[:150], beta[:150], ref_pool,
+                           np.array([0]), np.array([0, 150]), dtype=np.float64)
+    assert state_rel(got[0], ref_pool[0]) <= STATE_RTOL
+
+
 def test_chunk_then_decode_c0(ops):
     """Config 0 end to end on the core: prefill, then 16 decode steps."""
     c = I.C0
