@@ -74,24 +74,39 @@ __device__ __forceinline__ void decay_scan(ChunkScalars& s, int lane) {
   if ((lane & 7) == 7) s.gend[lane >> 3] = x;
 }
 
-// Row norms from the diagonal of P = [K;Q][K;Q]^T (TMEM columns colP..+128,
-// thread t <-> lane t of 128): nk = 1/|k|, nq = scale/|q| (l2norm eps 1e-6,
-// qwen3_5.py:160-161), cf = nk * bcol.
-__device__ __forceinline__ void norms_from_diag(ChunkScalars& s, uint32_t tl, uint32_t colP,
-                                                int tid, float scale) {
+// l2 norms (eps 1e-6, qwen3_5.py:160-161) of the chunk's rows, thread t <-> row
+// t of the [K;Q] tile (rows 0-63 K, 64-127 Q; two 64-column dk blocks).
+// K rows (t < 64): nk = 1/|k| from the diagonal of P = [K;Q] K^T (TMEM columns
+// colP.., exact bf16 products), cf = nk * bcol.
+__device__ __forceinline__ void k_norm_from_diag(ChunkScalars& s, uint32_t tl, uint32_t colP,
+                                                 int tid) {
   const int warp = tid >> 5, lane = tid & 31;
   float p[32];
   tmem_ld32(tl + colP + warp * 32, p);
   float d = 0.f;
 #pragma unroll
   for (int jj = 0; jj < 32; ++jj) d = (jj == lane) ? p[jj] : d;
-  if (tid < 64) {
-    const float n = rsqrtf(d + 1e-6f);
-    s.nk[tid] = n;
-    s.cf[tid] = n * s.bcol[tid];
-  } else {
-    s.nq[tid - 64] = rsqrtf(d + 1e-6f) * scale;
+  const float n = rsqrtf(d + 1e-6f);
+  s.nk[tid] = n;
+  s.cf[tid] = n * s.bcol[tid];
+}
+// Q rows (t >= 64): nq = scale/|q| summed on the CUDA cores in a fixed order
+// (rows past the sequence end count as zero rows).
+__device__ __forceinline__ void q_norm(ChunkScalars& s, const uint8_t* kq, int tid, int nv,
+                                       float scale) {
+  const int i = tid - 64;
+  float a0 = 0.f, a1 = 0.f;
+  if (i < nv) {
+#pragma unroll
+    for (int c = 0; c < 16; ++c) {
+      float f[8];
+      unpack8(*reinterpret_cast<const uint4*>(kq + (c >> 3) * 16384 + sw128(64 + i, (c & 7) * 8)),
+              f);
+#pragma unroll
+      for (int e = 0; e < 8; e += 2) ffma2(a0, a1, f[e], f[e + 1], f[e], f[e + 1], a0, a1);
+    }
   }
+  s.nq[i] = rsqrtf(a0 + a1 + 1e-6f) * scale;
 }
 
 // From P (TMEM, thread t <-> lane t of 128): rows 0-63 build
@@ -118,18 +133,26 @@ __device__ __forceinline__ void build_l_qkm(const ChunkScalars& s, uint32_t tl, 
       if (J < I) {
         const float rf = rowf * __expf(gi - s.gend[J]);
 #pragma unroll
-        for (int jj = 0; jj < 16; jj += 2) {
-          const float2 c2 = *reinterpret_cast<const float2*>(&s.cf[J * 16 + jj]);
-          float f0, f1;
-          fmul2(f0, f1, rf, rf, c2.x, c2.y);
+        for (int jj = 0; jj < 16; jj += 4) {
+          const float4 c4 = *reinterpret_cast<const float4*>(&s.cf[J * 16 + jj]);
+          float f0, f1, f2, f3;
+          fmul2(f0, f1, rf, rf, c4.x, c4.y);
+          fmul2(f2, f3, rf, rf, c4.z, c4.w);
           fmul2(pe[jj], pe[jj + 1], pe[jj], pe[jj + 1], f0, f1);
+          fmul2(pe[jj + 2], pe[jj + 3], pe[jj + 2], pe[jj + 3], f2, f3);
         }
       } else if (J == I) {
 #pragma unroll
-        for (int jj = 0; jj < 16; ++jj) {
-          const int j = J * 16 + jj;
-          const bool keep = isq ? (j <= i) : (j < i);
-          pe[jj] = keep ? pe[jj] * rowf * s.nk[j] * __expf(gi - s.gam[j]) : 0.f;
+        for (int j4 = 0; j4 < 16; j4 += 4) {
+          const float4 n4 = *reinterpret_cast<const float4*>(&s.nk[J * 16 + j4]);
+          const float4 g4 = *reinterpret_cast<const float4*>(&s.gam[J * 16 + j4]);
+          const float nv4[4] = {n4.x, n4.y, n4.z, n4.w}, gv4[4] = {g4.x, g4.y, g4.z, g4.w};
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const int jj = j4 + k, j = J * 16 + jj;
+            const bool keep = isq ? (j <= i) : (j < i);
+            pe[jj] = keep ? pe[jj] * rowf * nv4[k] * __expf(gi - gv4[k]) : 0.f;
+          }
         }
       } else {
 #pragma unroll
@@ -148,12 +171,66 @@ __device__ __forceinline__ void build_l_qkm(const ChunkScalars& s, uint32_t tl, 
   }
 }
 
+// m16n8k8 tf32 tensor-core tile product (warp-wide): D += A B, fp32 accumulate.
+__device__ __forceinline__ void mma_tf32(float (&d)[4], const uint32_t (&a)[4],
+                                         const uint32_t (&b)[2]) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k8.row.col.f32.tf32.tf32.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+      "{%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b[0]), "r"(b[1]));
+}
+// fp32 -> tf32 (round to nearest, ties away from zero).
+__device__ __forceinline__ uint32_t to_tf32(float x) {
+  uint32_t r;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+  return r;
+}
+
+// D[16 x 8*NT] = A[16 x 8*KS] B[8*KS x 8*NT] for one warp, A and B fp32 in
+// shared memory (row pitches lda / ldb floats), rounded to tf32 on load;
+// fragment layout of mma.m16n8k8 (g = lane / 4, t = lane % 4).
+template <int KS, int NT>
+__device__ __forceinline__ void warp_mma_tf32(float (&d)[NT][4], const float* A, int lda,
+                                              const float* B, int ldb, int lane) {
+  const int g = lane >> 2, t = lane & 3;
+#pragma unroll
+  for (int n = 0; n < NT; ++n) d[n][0] = d[n][1] = d[n][2] = d[n][3] = 0.f;
+#pragma unroll
+  for (int ks = 0; ks < KS; ++ks) {
+    const float* Ak = A + ks * 8;
+    const uint32_t a[4] = {to_tf32(Ak[g * lda + t]), to_tf32(Ak[(g + 8) * lda + t]),
+                           to_tf32(Ak[g * lda + t + 4]), to_tf32(Ak[(g + 8) * lda + t + 4])};
+    const float* Bk = B + ks * 8 * ldb;
+#pragma unroll
+    for (int n = 0; n < NT; ++n) {
+      const uint32_t bb[2] = {to_tf32(Bk[t * ldb + n * 8 + g]),
+                              to_tf32(Bk[(t + 4) * ldb + n * 8 + g])};
+      mma_tf32(d[n], a, bb);
+    }
+  }
+}
+template <int NT>
+__device__ __forceinline__ void warp_store_tile(const float (&d)[NT][4], float* D, int ldd,
+                                                int lane) {
+  const int g = lane >> 2, t = lane & 3;
+#pragma unroll
+  for (int n = 0; n < NT; ++n) {
+    *reinterpret_cast<float2*>(&D[g * ldd + n * 8 + 2 * t]) = make_float2(d[n][0], d[n][1]);
+    *reinterpret_cast<float2*>(&D[(g + 8) * ldd + n * 8 + 2 * t]) = make_float2(d[n][2], d[n][3]);
+  }
+}
+
+constexpr int kXP = 40;   // row pitch of the X scratch (conflict-free B-fragment reads)
+
 // T = (I - L)^-1 for the strictly lower 64x64 L (fp32, shared memory, upper
 // triangle zero), computed IN PLACE (T overwrites L): 16x16 diagonal blocks by
-// forward substitution in registers, then two recursive-doubling levels —
-// with (I - L) = [A 0; -L21 B], T = [A^-1 0; B^-1 L21 A^-1  B^-1] — at
-// 16 -> 32 and 32 -> 64.  Each level reads its L21 block before the T21 that
-// replaces it is written.  128 threads; X is a 4 KiB fp32 scratch.
+// forward substitution in registers (fp32), then two recursive-doubling levels
+// — with (I - L) = [A 0; -L21 B], T = [A^-1 0; B^-1 L21 A^-1  B^-1] — at
+// 16 -> 32 and 32 -> 64, their block products on the tensor cores (tf32
+// operands, fp32 accumulation; T is rounded to bf16 for its MMAs afterwards).
+// Each level reads its L21 block before the T21 that replaces it is written.
+// 128 threads (4 warps); X is a 5 KiB fp32 scratch (32 rows of kXP).
 __device__ __forceinline__ void invert_unit_lower(float (*LT)[kLP], float* X, int tid) {
   const int warp = tid >> 5, lane = tid & 31;
   {  // diagonal 16x16 blocks: warp w owns block w, lane l solves column l % 16
@@ -163,9 +240,17 @@ __device__ __forceinline__ void invert_unit_lower(float (*LT)[kLP], float* X, in
     for (int i = 0; i < 16; ++i) {
       float s0 = 0.f, s1 = 0.f;
 #pragma unroll
-      for (int m = 0; m < i; ++m) {
-        const float pr = LT[b0 + i][b0 + m] * t[m];
-        if (m & 1) s1 += pr; else s0 += pr;
+      for (int m4 = 0; m4 < (i + 3) / 4; ++m4) {
+        const float4 l4 = *reinterpret_cast<const float4*>(&LT[b0 + i][b0 + 4 * m4]);
+        const float lv[4] = {l4.x, l4.y, l4.z, l4.w};
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const int m = 4 * m4 + k;
+          if (m < i) {
+            const float pr = lv[k] * t[m];
+            if (m & 1) s1 += pr; else s0 += pr;
+          }
+        }
       }
       t[i] = (i == j) ? 1.f : (i > j ? s0 + s1 : 0.f);
     }
@@ -176,43 +261,25 @@ __device__ __forceinline__ void invert_unit_lower(float (*LT)[kLP], float* X, in
     }
   }
   __syncthreads();
-  {  // 16 -> 32: for both 32-blocks, X = L21 A^-1, then T21 = B^-1 X (4 outputs / thread)
-    const int hsel = tid >> 6, hb = hsel * 32, r = (tid >> 2) & 15, c0 = (tid & 3) * 4;
-    float* Xh = X + hsel * 256;
-    float a[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-    for (int s = 0; s < 16; ++s)
-      fma4(a, LT[hb + 16 + r][hb + s], *reinterpret_cast<const float4*>(&LT[hb + s][hb + c0]));
-    *reinterpret_cast<float4*>(&Xh[r * 16 + c0]) = make_float4(a[0], a[1], a[2], a[3]);
-    __syncthreads();
-    float b[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-    for (int s = 0; s < 16; ++s)
-      fma4(b, LT[hb + 16 + r][hb + 16 + s], *reinterpret_cast<const float4*>(&Xh[s * 16 + c0]));
-    *reinterpret_cast<float4*>(&LT[hb + 16 + r][hb + c0]) = make_float4(b[0], b[1], b[2], b[3]);
+  {  // 16 -> 32: warp w: 32-block hb = 32 (w / 2), column tile 8 (w % 2) of the 16-wide blocks
+    const int hb = (warp >> 1) * 32, c = (warp & 1) * 8;
+    float* Xh = X + (warp >> 1) * 16;
+    float d[1][4];
+    warp_mma_tf32<2, 1>(d, &LT[hb + 16][hb], kLP, &LT[hb][hb + c], kLP, lane);   // L21 A^-1
+    warp_store_tile<1>(d, Xh + c, kXP, lane);
+    __syncthreads();   // every warp has read its L21 block
+    warp_mma_tf32<2, 1>(d, &LT[hb + 16][hb + 16], kLP, Xh + c, kXP, lane);       // B^-1 X
+    warp_store_tile<1>(d, &LT[hb + 16][hb + c], kLP, lane);
   }
   __syncthreads();
-  {  // 32 -> 64: X = L21 A^-1 (32x32), then T21 = B^-1 X (8 outputs / thread)
-    const int rr = tid >> 2, c0 = (tid & 3) * 8;
-    float a0[4] = {0.f, 0.f, 0.f, 0.f}, a1[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll 8
-    for (int s = 0; s < 32; ++s) {
-      const float l = LT[32 + rr][s];
-      fma4(a0, l, *reinterpret_cast<const float4*>(&LT[s][c0]));
-      fma4(a1, l, *reinterpret_cast<const float4*>(&LT[s][c0 + 4]));
-    }
-    *reinterpret_cast<float4*>(&X[rr * 32 + c0]) = make_float4(a0[0], a0[1], a0[2], a0[3]);
-    *reinterpret_cast<float4*>(&X[rr * 32 + c0 + 4]) = make_float4(a1[0], a1[1], a1[2], a1[3]);
-    __syncthreads();
-    float b0[4] = {0.f, 0.f, 0.f, 0.f}, b1[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll 8
-    for (int s = 0; s < 32; ++s) {
-      const float t = LT[32 + rr][32 + s];
-      fma4(b0, t, *reinterpret_cast<const float4*>(&X[s * 32 + c0]));
-      fma4(b1, t, *reinterpret_cast<const float4*>(&X[s * 32 + c0 + 4]));
-    }
-    *reinterpret_cast<float4*>(&LT[32 + rr][c0]) = make_float4(b0[0], b0[1], b0[2], b0[3]);
-    *reinterpret_cast<float4*>(&LT[32 + rr][c0 + 4]) = make_float4(b1[0], b1[1], b1[2], b1[3]);
+  {  // 32 -> 64: warp w: rows 16 (w / 2) of the 32-row blocks, column tiles 2 (w % 2) + {0, 1}
+    const int r = (warp >> 1) * 16, c = (warp & 1) * 16;
+    float d[2][4];
+    warp_mma_tf32<4, 2>(d, &LT[32 + r][0], kLP, &LT[0][c], kLP, lane);          // L21 A^-1
+    warp_store_tile<2>(d, X + r * kXP + c, kXP, lane);
+    __syncthreads();   // X complete; every warp has read L21
+    warp_mma_tf32<4, 2>(d, &LT[32 + r][32], kLP, X + c, kXP, lane);             // B^-1 X
+    warp_store_tile<2>(d, &LT[32 + r][c], kLP, lane);
   }
   __syncthreads();
 }

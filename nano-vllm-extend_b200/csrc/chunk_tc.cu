@@ -49,7 +49,7 @@ constexpr uint32_t kTmemCols = 256;
 constexpr uint32_t kColS = 0, kColW = 128;
 
 // Shared memory (~106 KiB: two CTAs fit on an SM).  `scratch` is reused in
-// turn: L then T in place (fp32 [64][68]) plus X (fp32 32x32) during the
+// turn: L then T in place (fp32 [64][68]) plus X (fp32 32 x 40) during the
 // inverse; the bf16 S tile for MMA 3; then the R and W hi / lo tiles.
 struct __align__(1024) ChunkSmem {
   uint8_t kq[2][128 * 128];   // [dk block][row][128 B]: rows 0-63 K, rows 64-127 Q
@@ -250,7 +250,8 @@ __global__ void __launch_bounds__(kThreads, 2) chunk_prefill_tc_kernel(
       mma_commit(bar);
     }
     if (!(ok = wait_mma())) break;
-    norms_from_diag(sm.sc, tl, kColW, tid, scale);   // P[t][t]: the row norms
+    if (tid < 64) k_norm_from_diag(sm.sc, tl, kColW, tid);
+    else q_norm(sm.sc, sm.kq[0], tid, nv, scale);
     __syncthreads();
 
     // ---- L (rows 0-63) and QKm (rows 64-127) from P; then scale Q rows by e^gamma nq

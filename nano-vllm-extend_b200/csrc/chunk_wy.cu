@@ -105,19 +105,23 @@ __global__ void __launch_bounds__(kIndexThreads) chunk_index_kernel(
 }
 
 // ---------------------------------------------------------------- prep
-struct __align__(1024) PrepSmem {
-  uint8_t kq[2][128 * 128];   // [K;Q]; after MMA 1: L / T (fp32), X, the QKm tile
-  uint8_t a4[128 * 128];      // [T ; M2] (interleaved rows) } one block image,
-  float f[5][kC];             // the factors               } stored by one bulk copy
+// One 32 KiB region serves in turn as the [K;Q] tile (MMA 1), as L / T (fp32),
+// the QKm tile and X (the inverse), and as the [T; M2] block image (MMA 2 and
+// the store) — about 36 KiB per CTA, 64 TMEM columns: six CTAs per SM.
+struct PrepSmem {             // placed at a 1024-byte aligned base (r0's swizzle atoms)
+  uint8_t r0[32768];
+  float f[5][kC];             // the block's factors
   ChunkScalars sc;
   unsigned long long mbar, lbar;
   uint32_t tmem_base;
   int abort;
 };
-constexpr uint32_t kXOff = kC * kLP * 4;          // X after L / T (17,408 B)
-constexpr uint32_t kQkmOff = 21504;               // QKm tile (1024-aligned) after X
+constexpr uint32_t kQkmOff = 18432;   // QKm tile (1024-aligned) after L / T (17,408 B)
+constexpr uint32_t kXOff = 26624;     // X (5 KiB) after QKm; MMA 2's unused A rows 64-127
+                                      // read [26624, 34816): X and the arrays after r0
+constexpr int kPrepCtasPerSm = 6;
 
-__global__ void __launch_bounds__(kPrepThreads, 4) chunk_prep_kernel(
+__global__ void __launch_bounds__(kPrepThreads, kPrepCtasPerSm) chunk_prep_kernel(
     const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
     const float* __restrict__ g, const bf16* __restrict__ beta,
     const int2* __restrict__ chunk_info, int HK, int HV, float scale,
@@ -134,7 +138,7 @@ __global__ void __launch_bounds__(kPrepThreads, 4) chunk_prep_kernel(
   const int nv = info.y;
   if (nv <= 0) return;                   // past the last chunk
 
-  const uint32_t kq0 = smem_u32(sm.kq[0]);
+  const uint32_t r00 = smem_u32(sm.r0);
   const uint32_t bar = smem_u32(&sm.mbar), lbar = smem_u32(&sm.lbar);
   if (tid == 0) {
     mbar_init(bar, 1);
@@ -143,8 +147,8 @@ __global__ void __launch_bounds__(kPrepThreads, 4) chunk_prep_kernel(
     sm.abort = 0;
     mbar_expect_tx(lbar, 4 * 8192);
     for (int blk = 0; blk < 2; ++blk) {
-      tma_load_2d(kq0 + blk * 16384, &tm_k, hk * kD + blk * 64, (int)t0, lbar);
-      tma_load_2d(kq0 + blk * 16384 + 64 * 128, &tm_q, hk * kD + blk * 64, (int)t0, lbar);
+      tma_load_2d(r00 + blk * 16384, &tm_k, hk * kD + blk * 64, (int)t0, lbar);
+      tma_load_2d(r00 + blk * 16384 + 64 * 128, &tm_q, hk * kD + blk * 64, (int)t0, lbar);
     }
   }
   if (tid < kC) {
@@ -156,7 +160,7 @@ __global__ void __launch_bounds__(kPrepThreads, 4) chunk_prep_kernel(
     sm.sc.gam[tid] = gv;
     sm.sc.bet[tid] = bv;
   }
-  if (warp == 0) tmem_alloc(smem_u32(&sm.tmem_base), 128);
+  if (warp == 0) tmem_alloc(smem_u32(&sm.tmem_base), 64);
   fence_before();
   __syncthreads();
   fence_after();
@@ -178,8 +182,8 @@ __global__ void __launch_bounds__(kPrepThreads, 4) chunk_prep_kernel(
       for (int idx = tid; idx < (kC - nv) * 16; idx += kPrepThreads) {
         const int i = nv + idx / 16, ch = idx % 16, blk = ch >> 3, c8 = (ch & 7) * 8;
         const uint4 z = make_uint4(0, 0, 0, 0);
-        *reinterpret_cast<uint4*>(sm.kq[blk] + sw128(i, c8)) = z;
-        *reinterpret_cast<uint4*>(sm.kq[blk] + sw128(64 + i, c8)) = z;
+        *reinterpret_cast<uint4*>(sm.r0 + blk * 16384 + sw128(i, c8)) = z;
+        *reinterpret_cast<uint4*>(sm.r0 + blk * 16384 + sw128(64 + i, c8)) = z;
       }
     }
     if (warp == 0) decay_scan(sm.sc, lane);
@@ -187,31 +191,44 @@ __global__ void __launch_bounds__(kPrepThreads, 4) chunk_prep_kernel(
     fence_before();
     __syncthreads();
     fence_after();
-    // (1) P = [K;Q] [K;Q]^T : M = 128, N = 128, K = 128
+    // (1) P = [K;Q] K^T : M = 128, N = 64 (the K rows), K = 128
     if (tid == 0) {
 #pragma unroll
       for (int s = 0; s < 8; ++s) {
         const uint32_t off = (uint32_t)(s >> 2) * 16384u + (uint32_t)(s & 3) * 32u;
-        mma_bf16(tbase, smem_desc(kq0 + off, 16, 1024), smem_desc(kq0 + off, 16, 1024),
-                 idesc_bf16(128, 128, false, false), s > 0);
+        mma_bf16(tbase, smem_desc(r00 + off, 16, 1024), smem_desc(r00 + off, 16, 1024),
+                 idesc_bf16(128, 64, false, false), s > 0);
       }
       mma_commit(bar);
     }
+    if (tid >= 64) q_norm(sm.sc, sm.r0, tid, nv, scale);   // Q rows: CUDA cores, under MMA 1
     ok = wait1(bar, 0);
   }
   if (ok) {
-    norms_from_diag(sm.sc, tl, 0, tid, scale);
+    if (tid < 64) k_norm_from_diag(sm.sc, tl, 0, tid);    // K rows: P's diagonal
     __syncthreads();
-    uint8_t* const kqb = &sm.kq[0][0];                           // K / Q are consumed
-    float (*Lm)[kLP] = reinterpret_cast<float (*)[kLP]>(kqb);
-    float* Xs = reinterpret_cast<float*>(kqb + kXOff);
-    uint8_t* qkm = kqb + kQkmOff;
+    float (*Lm)[kLP] = reinterpret_cast<float (*)[kLP]>(sm.r0);     // K / Q are consumed
+    float* Xs = reinterpret_cast<float*>(sm.r0 + kXOff);
+    uint8_t* qkm = sm.r0 + kQkmOff;
     build_l_qkm(sm.sc, tl, 0, tid, Lm, qkm);
     __syncthreads();
     invert_unit_lower(Lm, Xs, tid);
-    for (int idx = tid; idx < kC * 8; idx += kPrepThreads) {
-      const int i = idx >> 3, c8 = (idx & 7) * 8;
-      st8(sm.a4, ilv_row(i, false), c8, &Lm[i][c8]);
+    {   // T (fp32, rows of 68) -> the bf16 T rows of the block image, over L / T
+      float t[4][8];
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const int idx = tid + k * kPrepThreads, i = idx >> 3, c8 = (idx & 7) * 8;
+        const float4 a = *reinterpret_cast<const float4*>(&Lm[i][c8]);
+        const float4 bb = *reinterpret_cast<const float4*>(&Lm[i][c8 + 4]);
+        t[k][0] = a.x; t[k][1] = a.y; t[k][2] = a.z; t[k][3] = a.w;
+        t[k][4] = bb.x; t[k][5] = bb.y; t[k][6] = bb.z; t[k][7] = bb.w;
+      }
+      __syncthreads();
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const int idx = tid + k * kPrepThreads, i = idx >> 3, c8 = (idx & 7) * 8;
+        st8(sm.r0, ilv_row(i, false), c8, t[k]);
+      }
     }
     fence_async_smem();
     fence_before();
@@ -219,38 +236,37 @@ __global__ void __launch_bounds__(kPrepThreads, 4) chunk_prep_kernel(
     fence_after();
     // (2) M2 = [QKm; *] T : M = 128 (rows 64-127 unused), N = 64, K = 64
     if (tid == 0) {
-      const uint32_t qkm0 = kq0 + kQkmOff, a40 = smem_u32(sm.a4);
 #pragma unroll
       for (int s = 0; s < 4; ++s)
-        mma_bf16(tbase, smem_desc(qkm0 + s * 32, 16, 1024),
-                 smem_desc(a40 + ilv_row(16 * s, false) * 128, 8192, 1024),
+        mma_bf16(tbase, smem_desc(r00 + kQkmOff + s * 32, 16, 1024),
+                 smem_desc(r00 + ilv_row(16 * s, false) * 128, 8192, 1024),
                  idesc_bf16(128, 64, false, true), s > 0);
       mma_commit(bar);
     }
-    if (tid < kC) {   // per-token factors of the chain's phases
-      const ChunkScalars& s = sm.sc;
-      sm.f[0][tid] = s.eg[tid] * s.nk[tid];                             // R: e^gamma nk
-      sm.f[1][tid] = s.bet[tid];                                        // R: beta
-      sm.f[2][tid] = s.eg[tid] * s.nq[tid];                             // QS: e^gamma nq
-      sm.f[3][tid] = s.nk[tid] * expf(s.gam[kC - 1] - s.gam[tid]);      // W: nk e^(gL - g)
-      sm.f[4][tid] = tid == 0 ? s.eg[kC - 1] : 0.f;                     // S: e^gamma_L
-    }
     ok = wait1(bar, 1);
     if (ok) {
-      if (tid < 64) {   // M2 rows -> the a4 rows of the second half
+      if (tid < 64) {   // M2 rows -> the image rows of the second half; the factors
 #pragma unroll
         for (int hh = 0; hh < 2; ++hh) {
           float m[32];
           tmem_ld32(tl + hh * 32, m);
 #pragma unroll
           for (int q8 = 0; q8 < 4; ++q8)
-            st8(sm.a4, ilv_row(tid, true), hh * 32 + q8 * 8, m + q8 * 8);
+            st8(sm.r0, ilv_row(tid, true), hh * 32 + q8 * 8, m + q8 * 8);
         }
+        const ChunkScalars& s = sm.sc;
+        sm.f[0][tid] = s.eg[tid] * s.nk[tid];                             // R: e^gamma nk
+        sm.f[1][tid] = s.bet[tid];                                        // R: beta
+        sm.f[2][tid] = s.eg[tid] * s.nq[tid];                             // QS: e^gamma nq
+        sm.f[3][tid] = s.nk[tid] * expf(s.gam[kC - 1] - s.gam[tid]);      // W: nk e^(gL - g)
+        sm.f[4][tid] = tid == 0 ? s.eg[kC - 1] : 0.f;                     // S: e^gamma_L
       }
       fence_async_smem();
       __syncthreads();
       if (tid == 0) {
-        bulk_store(blocks + ((int64_t)b * HV + h) * kBlockBytes, smem_u32(sm.a4), kBlockBytes);
+        uint8_t* dst = blocks + ((int64_t)b * HV + h) * kBlockBytes;
+        bulk_store(dst, r00, kTile);
+        bulk_store(dst + kTile, smem_u32(&sm.f[0][0]), kScal);
         bulk_wait_read();
       }
     }
@@ -258,7 +274,7 @@ __global__ void __launch_bounds__(kPrepThreads, 4) chunk_prep_kernel(
   fence_before();
   __syncthreads();
   fence_after();
-  if (warp == 0) tmem_dealloc(tbase, 128);
+  if (warp == 0) tmem_dealloc(tbase, 64);
 }
 
 // ---------------------------------------------------------------- chain
