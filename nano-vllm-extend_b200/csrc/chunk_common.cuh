@@ -122,7 +122,7 @@ __device__ __forceinline__ void build_l_qkm(const ChunkScalars& s, uint32_t tl, 
   const int I = i >> 4;
   const float gi = s.gam[i];
   const float rowf = isq ? s.nq[i] : -s.bet[i] * s.nk[i];
-#pragma unroll
+#pragma unroll 1   // rolled: the unrolled body's code size costs instruction-cache misses
   for (int hh = 0; hh < 2; ++hh) {
     float p[32];
     tmem_ld32(tl + colP + hh * 32, p);

@@ -283,9 +283,9 @@ struct __align__(1024) ChainSmem {
   uint8_t scratch[32768];     // the bf16 S tile for MMA 3, then R, then W (hi / lo)
   uint8_t a4[128 * 128];      // [T ; M2] from the chunk's block
   uint8_t v[2][64 * 128];     // [dv block][token row][128 B]
-  float f[5][kC];             // the block's per-token factors
+  float f[2][5][kC];          // the blocks' per-token factors, chunks c and c + 1
   unsigned long long mbar;    // MMA completion
-  unsigned long long lbar[4]; // loads: K, Q, V, block
+  unsigned long long lbar[5]; // loads: K, Q, V, [T;M2] tile, factors
   uint32_t tmem_base;
   int abort;
 };
@@ -354,29 +354,34 @@ __global__ void __launch_bounds__(kChainThreads, 2) chunk_chain_kernel(
     for (int blk = 0; blk < 2; ++blk)
       tma_load_2d(smem_u32(sm.v[blk]), &tm_v, h * kD + blk * 64, (int)(start + c * kC), b);
   };
-  auto load_blk = [&](int c) {
+  auto load_tile = [&](int c) {     // the [T; M2] tile of chunk c's block
     const uint32_t b = smem_u32(&sm.lbar[3]);
-    const uint8_t* src = blocks + ((int64_t)(cs + c) * HV + h) * kBlockBytes;
-    mbar_expect_tx(b, kBlockBytes);
-    bulk_load(smem_u32(sm.a4), src, kTile, b);
-    bulk_load(smem_u32(&sm.f[0][0]), src + kTile, kScal, b);
+    mbar_expect_tx(b, kTile);
+    bulk_load(smem_u32(sm.a4), blocks + ((int64_t)(cs + c) * HV + h) * kBlockBytes, kTile, b);
+  };
+  auto load_f = [&](int c) {        // the factors of chunk c's block, into buffer c % 2
+    const uint32_t b = smem_u32(&sm.lbar[4]);
+    mbar_expect_tx(b, kScal);
+    bulk_load(smem_u32(&sm.f[c & 1][0][0]),
+              blocks + ((int64_t)(cs + c) * HV + h) * kBlockBytes + kTile, kScal, b);
   };
 
   const uint32_t bar = smem_u32(&sm.mbar);
   if (tid == 0) {
     mbar_init(bar, 1);
-    for (int i = 0; i < 4; ++i) mbar_init(smem_u32(&sm.lbar[i]), 1);
+    for (int i = 0; i < 5; ++i) mbar_init(smem_u32(&sm.lbar[i]), 1);
     mbar_init_fence();
     sm.abort = 0;
   }
   __syncthreads();
   if (tid == 0) {
-    load_blk(0);
+    load_f(0);
     load_k(0);
     load_q(0);
+    load_tile(0);
     load_v(0);
   }
-  uint32_t lphase[4] = {0u, 0u, 0u, 0u};
+  uint32_t lphase[5] = {0u, 0u, 0u, 0u, 0u};
   if (warp == 0) tmem_alloc(smem_u32(&sm.tmem_base), 256);
   fence_before();
   __syncthreads();
@@ -439,14 +444,17 @@ __global__ void __launch_bounds__(kChainThreads, 2) chunk_chain_kernel(
     const int64_t t0 = start + (int64_t)c * kC;
     const int nv = (int)min((int64_t)kC, len - (int64_t)c * kC);
     const bool full = nv == kC;
-    if (tid == 0) wait_load(3);
+    if (tid == 0) wait_load(4);                    // the factors of chunk c
     __syncthreads();
     if (sm.abort) { ok = false; break; }
     const int i = (qd >> 1) * 32 + lane;            // token of this thread's tile row
-    const float f0 = sm.f[second ? 2 : 0][i];       // e^gamma nk (R rows) | e^gamma nq (QS rows)
-    const float bi = sm.f[1][i];
-    const float wk = sm.f[3][i];
-    const float egl = sm.f[4][0];
+    const float (&fc)[5][kC] = sm.f[c & 1];
+    const float f0 = fc[second ? 2 : 0][i];         // e^gamma nk (R rows) | e^gamma nq (QS rows)
+    const float bi = fc[1][i];
+    const float wk = fc[3][i];
+    const float egl = fc[4][0];
+    // the other buffer was last read in chunk c - 1 (barriers since): prefetch c + 1
+    if (tid == 0 && c + 1 < nchunks) load_f(c + 1);
 
     // S (state after the previous chunk) -> bf16 MN-major tile (row = dk,
     // col = dv) for MMA 3; then S *= e^gamma_L in TMEM for MMA 5
@@ -490,7 +498,13 @@ __global__ void __launch_bounds__(kChainThreads, 2) chunk_chain_kernel(
                  smem_desc(scr0 + s * 2048, 16384, 1024), idesc_bf16(128, 128, false, true), s > 0);
       mma_commit(bar);
     }
-    if (tid == 0) wait_load(2);                        // V, before the barrier in wait_mma
+    if (tid == 0) {
+      if (c > 0) {                 // the previous chunk's out tile has left a4: fetch [T; M2]
+        bulk_wait_read();
+        load_tile(c);
+      }
+      wait_load(2);                                    // V, before the barrier in wait_mma
+    }
     if (!(ok = wait_mma())) break;
     if (tid == 0 && c + 1 < nchunks) load_q(c + 1);   // Q rows are no longer read this chunk
 
@@ -531,7 +545,10 @@ __global__ void __launch_bounds__(kChainThreads, 2) chunk_chain_kernel(
       }
     }
     tmem_wait_st();
+    if (tid == 0) wait_load(3);                        // the [T; M2] tile of chunk c
     sync_for_mma();
+    if (sm.abort) { ok = false; break; }
+    if (tid == 0 && c + 1 < nchunks) load_v(c + 1);   // the v tile is consumed
 
     // ---- (4) W-region += [T;M2] [R_hi;R_lo] : T rows -> v', M2 rows -> out
     if (tid == 0) {
@@ -543,10 +560,9 @@ __global__ void __launch_bounds__(kChainThreads, 2) chunk_chain_kernel(
       mma_commit(bar);
     }
     if (!(ok = wait_mma())) break;
-    if (tid == 0 && c + 1 < nchunks) load_blk(c + 1);   // a4 and the factors are consumed
 
     // ---- epilogue: W = nk e^(gamma_L-gamma) v' (T rows); out (M2 rows) -> bf16
-    // tile in the (consumed) v buffer, stored by TMA while MMA 5 runs
+    // tile in the (consumed) a4 buffer, stored by TMA while MMA 5 runs
     {
       float vv[2][32];
       tmem_ld32x2(tl + kColW + c0, tl + kColW + c0 + 32, vv[0], vv[1]);
@@ -568,7 +584,7 @@ __global__ void __launch_bounds__(kChainThreads, 2) chunk_chain_kernel(
 #pragma unroll
           for (int q8 = 0; q8 < 4; ++q8) {
             if (full) {
-              st8(sm.v[half], i, cg * 32 + q8 * 8, vv[cg] + q8 * 8);
+              st8(sm.a4 + half * 8192, i, cg * 32 + q8 * 8, vv[cg] + q8 * 8);
             } else {   // a partial last chunk: rows past the end belong to the next sequence
               *reinterpret_cast<uint4*>(out + ((t0 + i) * HV + h) * kD + c0 + cg * 32 + q8 * 8) =
                   pack8(vv[cg] + q8 * 8);
@@ -588,20 +604,16 @@ __global__ void __launch_bounds__(kChainThreads, 2) chunk_chain_kernel(
       mma_commit(bar);
       if (full) {
         for (int blk = 0; blk < 2; ++blk)
-          tma_store_2d(&tm_out, h * kD + blk * 64, (int)t0, smem_u32(sm.v[blk]));
+          tma_store_2d(&tm_out, h * kD + blk * 64, (int)t0, a40 + blk * 8192);
         bulk_commit();
       }
     }
     if (!(ok = wait_mma())) break;
-    if (tid == 0 && c + 1 < nchunks) {
-      load_k(c + 1);                                  // the K rows are free
-      bulk_wait_read();                               // the out tile has left the v buffer
-      load_v(c + 1);
-    }
+    if (tid == 0 && c + 1 < nchunks) load_k(c + 1);   // the K rows are free
   }
   if (!ok && tid == 0) {   // drain loads still in flight before the CTA exits (bounded)
 #pragma unroll
-    for (int i = 0; i < 4; ++i) mbar_wait(smem_u32(&sm.lbar[i]), lphase[i], kSpin);
+    for (int i = 0; i < 5; ++i) mbar_wait(smem_u32(&sm.lbar[i]), lphase[i], kSpin);
   }
   if (tid == 0) bulk_wait_all();   // out tiles written before the CTA leaves
   if (ok) {   // final state -> pool slot
