@@ -464,14 +464,26 @@ def prefill_bench(pkg, device, steps, peaks):
         torch.cuda.synchronize()
         clocks = Clocks(device.index if device.index is not None else 0)
         clocks.start()
+        csteps = max(steps, 50)            # ~0.3 s: long enough for the clock sampler
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record()
-        for _ in range(steps):
+        for _ in range(csteps):
             pkg.ops.chunk_gated_delta_rule_varlen(q, k, v, gg, beta, m.s_cache, ids, cu,
                                                   max(lens))
         e1.record()
         torch.cuda.synchronize()
         chunk_clk = clocks.stop()
+        # the one-kernel form (no workspace), for comparison
+        pkg.ops.chunk_gated_delta_rule_varlen(q, k, v, gg, beta, m.s_cache, ids, cu, max(lens),
+                                              split=False)
+        torch.cuda.synchronize()
+        s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s0.record()
+        for _ in range(steps):
+            pkg.ops.chunk_gated_delta_rule_varlen(q, k, v, gg, beta, m.s_cache, ids, cu,
+                                                  max(lens), split=False)
+        s1.record()
+        torch.cuda.synchronize()
         o = pkg.ops.chunk_gated_delta_rule_varlen(q, k, v, gg, beta, m.s_cache, ids, cu,
                                                   max(lens))
         pkg.ops.rms_norm_gated(o, z, m.norm.weight, 1e-6)
@@ -484,7 +496,7 @@ def prefill_bench(pkg, device, steps, peaks):
         torch.cuda.synchronize()
     tn = n0.elapsed_time(n1) / 1e3 / steps
     norm_bytes = 3 * N * c["HV"] * c["DV"] * 2
-    tk = e0.elapsed_time(e1) / 1e3 / steps
+    tk = e0.elapsed_time(e1) / 1e3 / csteps
     flops = CHUNK_FLOPS_PER_TOKEN_HEAD * N * c["HV"]
     achieved = flops / tk / 1e12
     return {"workload": "config2: 1 GDN layer, 64 seqs, lens U[128,8192] seed 2, "
@@ -495,9 +507,13 @@ def prefill_bench(pkg, device, steps, peaks):
                             "ms": round(tn * 1e3, 3), "bound": "hbm",
                             "achieved": round(norm_bytes / tn / 1e9, 1), "unit": "GB/s",
                             "frac": round(norm_bytes / tn / 1e9 / peaks["hbm_gbs"], 4)},
-            "chunk_kernel": {"kernel": "chunk_prefill_tc_kernel",
+            "chunk_kernel": {"kernel": "chunk_index_kernel + chunk_prep_kernel + "
+                                       "chunk_chain_kernel (split form, one call)",
                              "bound": "tensor",
                              "ms": round(tk * 1e3, 3), "tok_s": round(N / tk, 1),
+                             "one_kernel_form_ms": round(s0.elapsed_time(s1) / steps, 3),
+                             "workspace_bytes": pkg.ops.chunk_prefill_workspace_bytes(
+                                 N, c["n_seqs"], c["HV"], c["DK"], c["DV"]),
                              "achieved": round(achieved, 2), "unit": "TFLOP/s",
                              "peak": peaks["bf16_tflops"], "peak_source": peaks["source"],
                              "frac": round(achieved / peaks["bf16_tflops"], 5),

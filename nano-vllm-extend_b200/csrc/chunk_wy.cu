@@ -4,8 +4,9 @@
 //
 //   chunk_index_kernel  chunk_start[r] = sum over earlier sequences of
 //                       ceil(len / 64) (the workspace's block numbering)
-//   chunk_prep_kernel   one CTA (128 threads, four per SM) per (chunk, v-head):
-//                       P = [K;Q][K;Q]^T on the tensor core, the l2 norms, the
+//   chunk_prep_kernel   one CTA (two warpgroups, three per SM) per (chunk, pair
+//                       of v-heads): P = [K;Q] K^T on the tensor core (once per
+//                       k-head), the l2 norms, the
 //                       decays, L and QKm, T = (I - L)^-1 (fp32), M2 = QKm T;
 //                       writes one 17,664-byte block: the [T; M2] tile as the
 //                       128B-swizzled shared-memory image MMA 4 reads, and the
@@ -31,7 +32,7 @@ constexpr uint32_t kSpin = 1u << 22;
 constexpr uint32_t kTile = 16384;                  // [T; M2]: 128 rows x 128 B
 constexpr uint32_t kScal = 5 * kC * 4;             // xs, beta, fq, wk, (e^gamma_L, 0 ...)
 constexpr uint32_t kBlockBytes = kTile + kScal;    // 17,664 (a multiple of 128)
-constexpr int kPrepThreads = 128;
+constexpr int kPrepThreads = 256;
 constexpr int kChainThreads = 256;
 constexpr int kIndexThreads = 1024;
 
@@ -105,21 +106,25 @@ __global__ void __launch_bounds__(kIndexThreads) chunk_index_kernel(
 }
 
 // ---------------------------------------------------------------- prep
-// One 32 KiB region serves in turn as the [K;Q] tile (MMA 1), as L / T (fp32),
-// the QKm tile and X (the inverse), and as the [T; M2] block image (MMA 2 and
-// the store) — about 36 KiB per CTA, 64 TMEM columns: six CTAs per SM.
-struct PrepSmem {             // placed at a 1024-byte aligned base (r0's swizzle atoms)
-  uint8_t r0[32768];
-  float f[5][kC];             // the block's factors
-  ChunkScalars sc;
+// One CTA (256 threads = two warpgroups) per (chunk, pair of v-heads 2p, 2p + 1);
+// warpgroup w handles v-head 2p + w.  When the two heads share a k-head (GQA),
+// the [K;Q] tile, P = [K;Q] K^T and the l2 norms are made once for both; else
+// each warpgroup loads its own tile.  Each warpgroup's 32 KiB region serves in
+// turn as its [K;Q] tile, as L / T (fp32), the QKm tile and X (the inverse),
+// and as its [T; M2] block image (MMA 2 and the store) — about 71 KiB and 128
+// TMEM columns per CTA: three CTAs (six heads) per SM.
+struct PrepSmem {             // placed at a 1024-byte aligned base (swizzle atoms)
+  uint8_t r[2][32768];
+  float f[2][5][kC];          // the blocks' factors
+  ChunkScalars sc[2];
   unsigned long long mbar, lbar;
   uint32_t tmem_base;
   int abort;
 };
 constexpr uint32_t kQkmOff = 18432;   // QKm tile (1024-aligned) after L / T (17,408 B)
 constexpr uint32_t kXOff = 26624;     // X (5 KiB) after QKm; MMA 2's unused A rows 64-127
-                                      // read [26624, 34816): X and the arrays after r0
-constexpr int kPrepCtasPerSm = 6;
+                                      // read [26624, 34816) of the region: don't-care data
+constexpr int kPrepCtasPerSm = 3;
 
 __global__ void __launch_bounds__(kPrepThreads, kPrepCtasPerSm) chunk_prep_kernel(
     const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
@@ -130,42 +135,55 @@ __global__ void __launch_bounds__(kPrepThreads, kPrepCtasPerSm) chunk_prep_kerne
   PrepSmem& sm = *reinterpret_cast<PrepSmem*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int b = blockIdx.x / HV;
-  const int h = blockIdx.x - b * HV;
-  const int hk = h / (HV / HK);
+  const int wg = tid >> 7, lt = tid & 127;           // warpgroup, thread within it
+  const int n_pairs = (HV + 1) >> 1;
+  const int b = blockIdx.x / n_pairs;
+  const int pair = blockIdx.x - b * n_pairs;
+  const int R = HV / HK;
+  const int h0 = 2 * pair, h1 = h0 + 1;
+  const bool has1 = h1 < HV;
+  const int hk0 = h0 / R, hk1 = has1 ? h1 / R : hk0;
+  const bool own1 = has1 && hk1 != hk0;             // head 1 needs its own [K;Q] tile
+  const int h = wg ? (has1 ? h1 : h0) : h0;         // this warpgroup's head
   const int2 info = chunk_info[b];
   const int64_t t0 = info.x;
   const int nv = info.y;
-  if (nv <= 0) return;                   // past the last chunk
+  if (nv <= 0) return;                               // past the last chunk
 
-  const uint32_t r00 = smem_u32(sm.r0);
+  uint8_t* const rw = sm.r[wg];                      // this warpgroup's region
+  const uint32_t r0s = smem_u32(sm.r[0]), r1s = smem_u32(sm.r[1]);
   const uint32_t bar = smem_u32(&sm.mbar), lbar = smem_u32(&sm.lbar);
   if (tid == 0) {
     mbar_init(bar, 1);
     mbar_init(lbar, 1);
     mbar_init_fence();
     sm.abort = 0;
-    mbar_expect_tx(lbar, 4 * 8192);
+    mbar_expect_tx(lbar, (own1 ? 2 : 1) * 4 * 8192);
     for (int blk = 0; blk < 2; ++blk) {
-      tma_load_2d(r00 + blk * 16384, &tm_k, hk * kD + blk * 64, (int)t0, lbar);
-      tma_load_2d(r00 + blk * 16384 + 64 * 128, &tm_q, hk * kD + blk * 64, (int)t0, lbar);
+      tma_load_2d(r0s + blk * 16384, &tm_k, hk0 * kD + blk * 64, (int)t0, lbar);
+      tma_load_2d(r0s + blk * 16384 + 64 * 128, &tm_q, hk0 * kD + blk * 64, (int)t0, lbar);
+      if (own1) {
+        tma_load_2d(r1s + blk * 16384, &tm_k, hk1 * kD + blk * 64, (int)t0, lbar);
+        tma_load_2d(r1s + blk * 16384 + 64 * 128, &tm_q, hk1 * kD + blk * 64, (int)t0, lbar);
+      }
     }
   }
-  if (tid < kC) {
+  if (lt < kC) {
     float gv = 0.f, bv = 0.f;
-    if (tid < nv) {
-      gv = __ldg(g + (t0 + tid) * HV + h);
-      bv = __bfloat162float(beta[(t0 + tid) * HV + h]);
+    if (lt < nv) {
+      gv = __ldg(g + (t0 + lt) * HV + h);
+      bv = __bfloat162float(beta[(t0 + lt) * HV + h]);
     }
-    sm.sc.gam[tid] = gv;
-    sm.sc.bet[tid] = bv;
+    sm.sc[wg].gam[lt] = gv;
+    sm.sc[wg].bet[lt] = bv;
   }
-  if (warp == 0) tmem_alloc(smem_u32(&sm.tmem_base), 64);
+  if (warp == 0) tmem_alloc(smem_u32(&sm.tmem_base), 128);
   fence_before();
   __syncthreads();
   fence_after();
   const uint32_t tbase = sm.tmem_base;
-  const uint32_t tl = tbase + ((uint32_t)(warp * 32) << 16);
+  const uint32_t tl = tbase + ((uint32_t)((warp & 3) * 32) << 16);   // lane quarter warp % 4
+  const uint32_t colP = own1 ? 64u * wg : 0u;        // this head's P columns
   // one thread waits on each barrier; the others wait at the CTA barrier
   auto wait1 = [&](uint32_t mb, uint32_t ph) -> bool {
     if (tid == 0 && !mbar_wait(mb, ph, kSpin)) {
@@ -179,45 +197,61 @@ __global__ void __launch_bounds__(kPrepThreads, kPrepCtasPerSm) chunk_prep_kerne
   bool ok = wait1(lbar, 0);
   if (ok) {
     if (nv < kC) {   // rows past the sequence end: zero K and Q
-      for (int idx = tid; idx < (kC - nv) * 16; idx += kPrepThreads) {
-        const int i = nv + idx / 16, ch = idx % 16, blk = ch >> 3, c8 = (ch & 7) * 8;
+      const int nt = own1 ? 2 : 1;
+      for (int idx = tid; idx < nt * (kC - nv) * 16; idx += kPrepThreads) {
+        const int t = idx / ((kC - nv) * 16), rem = idx - t * (kC - nv) * 16;
+        const int i = nv + rem / 16, ch = rem % 16, blk = ch >> 3, c8 = (ch & 7) * 8;
         const uint4 z = make_uint4(0, 0, 0, 0);
-        *reinterpret_cast<uint4*>(sm.r0 + blk * 16384 + sw128(i, c8)) = z;
-        *reinterpret_cast<uint4*>(sm.r0 + blk * 16384 + sw128(64 + i, c8)) = z;
+        *reinterpret_cast<uint4*>(sm.r[t] + blk * 16384 + sw128(i, c8)) = z;
+        *reinterpret_cast<uint4*>(sm.r[t] + blk * 16384 + sw128(64 + i, c8)) = z;
       }
     }
-    if (warp == 0) decay_scan(sm.sc, lane);
+    if ((warp & 3) == 0) decay_scan(sm.sc[wg], lane);   // warps 0 and 4: one head each
     fence_async_smem();
     fence_before();
     __syncthreads();
     fence_after();
-    // (1) P = [K;Q] K^T : M = 128, N = 64 (the K rows), K = 128
+    // (1) P = [K;Q] K^T : M = 128, N = 64 (the K rows), K = 128; once per k-head
     if (tid == 0) {
 #pragma unroll
-      for (int s = 0; s < 8; ++s) {
-        const uint32_t off = (uint32_t)(s >> 2) * 16384u + (uint32_t)(s & 3) * 32u;
-        mma_bf16(tbase, smem_desc(r00 + off, 16, 1024), smem_desc(r00 + off, 16, 1024),
-                 idesc_bf16(128, 64, false, false), s > 0);
+      for (int t = 0; t < 2; ++t) {
+        if (t == 1 && !own1) break;
+        const uint32_t rs = t ? r1s : r0s;
+#pragma unroll
+        for (int s = 0; s < 8; ++s) {
+          const uint32_t off = (uint32_t)(s >> 2) * 16384u + (uint32_t)(s & 3) * 32u;
+          mma_bf16(tbase + 64u * t, smem_desc(rs + off, 16, 1024), smem_desc(rs + off, 16, 1024),
+                   idesc_bf16(128, 64, false, false), s > 0);
+        }
       }
       mma_commit(bar);
     }
-    if (tid >= 64) q_norm(sm.sc, sm.r0, tid, nv, scale);   // Q rows: CUDA cores, under MMA 1
+    if (lt >= 64 && (wg == 0 || own1))          // Q rows: CUDA cores, under MMA 1
+      q_norm(sm.sc[wg], rw, lt, nv, scale);
     ok = wait1(bar, 0);
   }
   if (ok) {
-    if (tid < 64) k_norm_from_diag(sm.sc, tl, 0, tid);    // K rows: P's diagonal
+    if (lt < 64 && (wg == 0 || own1)) k_norm_from_diag(sm.sc[wg], tl, colP, lt);   // P's diagonal
     __syncthreads();
-    float (*Lm)[kLP] = reinterpret_cast<float (*)[kLP]>(sm.r0);     // K / Q are consumed
-    float* Xs = reinterpret_cast<float*>(sm.r0 + kXOff);
-    uint8_t* qkm = sm.r0 + kQkmOff;
-    build_l_qkm(sm.sc, tl, 0, tid, Lm, qkm);
+    if (wg == 1 && !own1) {                      // head 1 shares head 0's norms
+      if (lt < 64) {
+        sm.sc[1].nk[lt] = sm.sc[0].nk[lt];
+        sm.sc[1].cf[lt] = sm.sc[0].nk[lt] * sm.sc[1].bcol[lt];
+      } else {
+        sm.sc[1].nq[lt - 64] = sm.sc[0].nq[lt - 64];
+      }
+    }
     __syncthreads();
-    invert_unit_lower(Lm, Xs, tid);
+    float (*Lm)[kLP] = reinterpret_cast<float (*)[kLP]>(rw);     // K / Q are consumed
+    float* Xs = reinterpret_cast<float*>(rw + kXOff);
+    build_l_qkm(sm.sc[wg], tl, colP, lt, Lm, rw + kQkmOff);
+    __syncthreads();
+    invert_unit_lower(Lm, Xs, lt);               // both warpgroups pass its barriers together
     {   // T (fp32, rows of 68) -> the bf16 T rows of the block image, over L / T
       float t[4][8];
 #pragma unroll
       for (int k = 0; k < 4; ++k) {
-        const int idx = tid + k * kPrepThreads, i = idx >> 3, c8 = (idx & 7) * 8;
+        const int idx = lt + k * 128, i = idx >> 3, c8 = (idx & 7) * 8;
         const float4 a = *reinterpret_cast<const float4*>(&Lm[i][c8]);
         const float4 bb = *reinterpret_cast<const float4*>(&Lm[i][c8 + 4]);
         t[k][0] = a.x; t[k][1] = a.y; t[k][2] = a.z; t[k][3] = a.w;
@@ -226,47 +260,54 @@ __global__ void __launch_bounds__(kPrepThreads, kPrepCtasPerSm) chunk_prep_kerne
       __syncthreads();
 #pragma unroll
       for (int k = 0; k < 4; ++k) {
-        const int idx = tid + k * kPrepThreads, i = idx >> 3, c8 = (idx & 7) * 8;
-        st8(sm.r0, ilv_row(i, false), c8, t[k]);
+        const int idx = lt + k * 128, i = idx >> 3, c8 = (idx & 7) * 8;
+        st8(rw, ilv_row(i, false), c8, t[k]);
       }
     }
     fence_async_smem();
     fence_before();
     __syncthreads();
     fence_after();
-    // (2) M2 = [QKm; *] T : M = 128 (rows 64-127 unused), N = 64, K = 64
+    // (2) M2 = [QKm; *] T per head : M = 128 (rows 64-127 unused), N = 64, K = 64
     if (tid == 0) {
 #pragma unroll
-      for (int s = 0; s < 4; ++s)
-        mma_bf16(tbase, smem_desc(r00 + kQkmOff + s * 32, 16, 1024),
-                 smem_desc(r00 + ilv_row(16 * s, false) * 128, 8192, 1024),
-                 idesc_bf16(128, 64, false, true), s > 0);
+      for (int t = 0; t < 2; ++t) {
+        const uint32_t rs = t ? r1s : r0s;
+#pragma unroll
+        for (int s = 0; s < 4; ++s)
+          mma_bf16(tbase + 64u * t, smem_desc(rs + kQkmOff + s * 32, 16, 1024),
+                   smem_desc(rs + ilv_row(16 * s, false) * 128, 8192, 1024),
+                   idesc_bf16(128, 64, false, true), s > 0);
+      }
       mma_commit(bar);
     }
     ok = wait1(bar, 1);
     if (ok) {
-      if (tid < 64) {   // M2 rows -> the image rows of the second half; the factors
+      if (lt < 64) {   // M2 rows -> the image rows of the second half; the factors
 #pragma unroll
         for (int hh = 0; hh < 2; ++hh) {
           float m[32];
-          tmem_ld32(tl + hh * 32, m);
+          tmem_ld32(tl + 64u * wg + hh * 32, m);
 #pragma unroll
           for (int q8 = 0; q8 < 4; ++q8)
-            st8(sm.r0, ilv_row(tid, true), hh * 32 + q8 * 8, m + q8 * 8);
+            st8(rw, ilv_row(lt, true), hh * 32 + q8 * 8, m + q8 * 8);
         }
-        const ChunkScalars& s = sm.sc;
-        sm.f[0][tid] = s.eg[tid] * s.nk[tid];                             // R: e^gamma nk
-        sm.f[1][tid] = s.bet[tid];                                        // R: beta
-        sm.f[2][tid] = s.eg[tid] * s.nq[tid];                             // QS: e^gamma nq
-        sm.f[3][tid] = s.nk[tid] * expf(s.gam[kC - 1] - s.gam[tid]);      // W: nk e^(gL - g)
-        sm.f[4][tid] = tid == 0 ? s.eg[kC - 1] : 0.f;                     // S: e^gamma_L
+        const ChunkScalars& s = sm.sc[wg];
+        float (&f)[5][kC] = sm.f[wg];
+        f[0][lt] = s.eg[lt] * s.nk[lt];                             // R: e^gamma nk
+        f[1][lt] = s.bet[lt];                                       // R: beta
+        f[2][lt] = s.eg[lt] * s.nq[lt];                             // QS: e^gamma nq
+        f[3][lt] = s.nk[lt] * expf(s.gam[kC - 1] - s.gam[lt]);      // W: nk e^(gL - g)
+        f[4][lt] = lt == 0 ? s.eg[kC - 1] : 0.f;                    // S: e^gamma_L
       }
       fence_async_smem();
       __syncthreads();
       if (tid == 0) {
-        uint8_t* dst = blocks + ((int64_t)b * HV + h) * kBlockBytes;
-        bulk_store(dst, r00, kTile);
-        bulk_store(dst + kTile, smem_u32(&sm.f[0][0]), kScal);
+        for (int t = 0; t < (has1 ? 2 : 1); ++t) {
+          uint8_t* dst = blocks + ((int64_t)b * HV + h0 + t) * kBlockBytes;
+          bulk_store(dst, t ? r1s : r0s, kTile);
+          bulk_store(dst + kTile, smem_u32(&sm.f[t][0][0]), kScal);
+        }
         bulk_wait_read();
       }
     }
@@ -274,7 +315,7 @@ __global__ void __launch_bounds__(kPrepThreads, kPrepCtasPerSm) chunk_prep_kerne
   fence_before();
   __syncthreads();
   fence_after();
-  if (warp == 0) tmem_dealloc(tbase, 64);
+  if (warp == 0) tmem_dealloc(tbase, 128);
 }
 
 // ---------------------------------------------------------------- chain
@@ -685,7 +726,7 @@ int chunk_prefill_wy(int n_seqs, int HV, cudaStream_t s, const bf16* q, int64_t 
                                                          chunk_start, chunk_info);
   int rc = check_launch("gdn_chunk_prefill_varlen");
   if (rc != GDN_OK || cap == 0) return rc;
-  wy::chunk_prep_kernel<<<(unsigned)(cap * HV), wy::kPrepThreads, prep_smem, s>>>(
+  wy::chunk_prep_kernel<<<(unsigned)(cap * ((HV + 1) / 2)), wy::kPrepThreads, prep_smem, s>>>(
       tm_q, tm_k, g, beta, chunk_info, HK, HV, scale, blocks, status);
   if ((rc = check_launch("gdn_chunk_prefill_varlen")) != GDN_OK) return rc;
   wy::chunk_chain_kernel<<<(unsigned)((int64_t)n_seqs * HV), wy::kChainThreads, chain_smem, s>>>(

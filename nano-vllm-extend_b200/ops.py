@@ -279,6 +279,27 @@ def chunk_prefill_workspace_bytes(n_tokens: int, n_seqs: int, HV: int, DK: int, 
     return int(_lib.load().gdn_chunk_prefill_workspace_bytes(n_tokens, n_seqs, HV, DK, DV))
 
 
+_CHUNK_WS: dict[tuple, torch.Tensor] = {}
+
+
+def chunk_workspace(device, nbytes: int) -> torch.Tensor:
+    """The split chunk prefill's scratch for the current stream of ``device``:
+    at least ``nbytes``, kept between calls and grown when a larger prefill
+    arrives (a multi-GB request per call can make the caching allocator go to
+    cudaMalloc next to a large resident pool).  One buffer per stream, so calls
+    on different streams never share it; a call uses it only in stream order."""
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    key = (idx, torch.cuda.current_stream(idx).cuda_stream)
+    t = _CHUNK_WS.get(key)
+    if t is None or t.numel() < nbytes:
+        _CHUNK_WS.pop(key, None)
+        t = None
+        with torch.inference_mode(False):
+            t = torch.empty(nbytes, dtype=torch.uint8, device=torch.device("cuda", idx))
+        _CHUNK_WS[key] = t
+    return t
+
+
 def chunk_gated_delta_rule_varlen(q, k, v, g, beta, s_pool, ids, cu_seqlens,
                                   max_seqlen: int, z=None, norm_weight=None,
                                   eps: float = 1e-6, out=None,
@@ -289,9 +310,9 @@ def chunk_gated_delta_rule_varlen(q, k, v, g, beta, s_pool, ids, cu_seqlens,
     views allowed), g fp32 / beta bf16 [N, HV].  Returns out [N, HV, DV]; with ``z`` /
     ``norm_weight`` the gated RMSNorm is fused as in
     :func:`recurrent_gdn_inplace`.  ``split`` (head dim 128) runs the split
-    form with a workspace from torch's caching allocator, as the reference
-    allocates its chunk intermediates per call; False runs the one-kernel
-    form (same bits, no workspace)."""
+    form with the per-stream workspace of :func:`chunk_workspace` (the
+    reference allocates its chunk intermediates per call); False runs the
+    one-kernel form (same bits, no workspace)."""
     _cuda(q, k, v, g, beta, s_pool, ids, cu_seqlens)
     N, HK, DK, qs = _heads(q, "q")
     N_k, HK_k, DK_k, ks = _heads(k, "k")
@@ -308,7 +329,8 @@ def chunk_gated_delta_rule_varlen(q, k, v, g, beta, s_pool, ids, cu_seqlens,
     z3, zs, nw = _norm_args(z, norm_weight, N, HV, DV)
     out = _out_buffer(out, (N, HV, DV), v.device)
     ws_bytes = chunk_prefill_workspace_bytes(N, ids.numel(), HV, DK, DV) if split else 0
-    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=v.device) if ws_bytes else None
+    ws = chunk_workspace(v.device, ws_bytes) if ws_bytes else None
+    ws_bytes = ws.numel() if ws is not None else 0
     rc = _lib.load().gdn_chunk_prefill_varlen(
         _p(q), qs, _p(k), ks, _p(v), vs, _p(g), _p(beta), _p(s_pool), _slot_stride(s_pool),
         s_pool.shape[0], _p(ids), _p(cu), ids.numel(), N, int(max_seqlen), _p(out), HK, HV, DK,
