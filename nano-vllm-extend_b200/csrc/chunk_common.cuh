@@ -32,8 +32,10 @@ __device__ __forceinline__ void split8(const float* x, uint8_t* tile_hi, uint8_t
   for (int e = 0; e < 4; ++e) {
     const uint32_t b0 = __float_as_uint(x[2 * e]), b1 = __float_as_uint(x[2 * e + 1]);
     hp[e] = __byte_perm(b0, b1, 0x7632);
-    lp[e] = __floats2bfloat162_rn(x[2 * e] - __uint_as_float(b0 & 0xFFFF0000u),
-                                  x[2 * e + 1] - __uint_as_float(b1 & 0xFFFF0000u));
+    float l0, l1;   // x - hi, exact, as one packed fp32x2 operation
+    ffma2(l0, l1, __uint_as_float(b0 & 0xFFFF0000u), __uint_as_float(b1 & 0xFFFF0000u), -1.f,
+          -1.f, x[2 * e], x[2 * e + 1]);
+    lp[e] = __floats2bfloat162_rn(l0, l1);
   }
   *reinterpret_cast<uint4*>(tile_hi + off) = h;
   *reinterpret_cast<uint4*>(tile_lo + off) = l;

@@ -29,6 +29,10 @@ namespace tc {
 namespace wy {
 
 constexpr uint32_t kSpin = 1u << 22;
+// The chain's loads are issued by one thread of warp 1 (a Q-row warp, light in
+// the R phase); thread 0 issues the MMAs, the output stores and does the waits,
+// so a TMA issue (hundreds of cycles for four boxes) never delays an MMA.
+constexpr int kLoader = 32;
 constexpr uint32_t kTile = 16384;                  // [T; M2]: 128 rows x 128 B
 constexpr uint32_t kScal = 5 * kC * 4;             // xs, beta, fq, wk, (e^gamma_L, 0 ...)
 constexpr uint32_t kBlockBytes = kTile + kScal;    // 17,664 (a multiple of 128)
@@ -495,7 +499,13 @@ __global__ void __launch_bounds__(kChainThreads, 2) chunk_chain_kernel(
     const float wk = fc[3][i];
     const float egl = fc[4][0];
     // the other buffer was last read in chunk c - 1 (barriers since): prefetch c + 1
-    if (tid == 0 && c + 1 < nchunks) load_f(c + 1);
+    if (tid == kLoader && c + 1 < nchunks) {
+      load_f(c + 1);
+      // the next K into L2: its tile load has to wait for MMA 5
+      for (int blk = 0; blk < 2; ++blk)
+        for (int hf = 0; hf < 2; ++hf)
+          tma_prefetch_2d(&tm_k, hk * kD + blk * 64, (int)(start + (c + 1) * kC + 32 * hf));
+    }
 
     // S (state after the previous chunk) -> bf16 MN-major tile (row = dk,
     // col = dv) for MMA 3; then S *= e^gamma_L in TMEM for MMA 5
@@ -547,7 +557,7 @@ __global__ void __launch_bounds__(kChainThreads, 2) chunk_chain_kernel(
       wait_load(2);                                    // V, before the barrier in wait_mma
     }
     if (!(ok = wait_mma())) break;
-    if (tid == 0 && c + 1 < nchunks) load_q(c + 1);   // Q rows are no longer read this chunk
+    if (tid == kLoader && c + 1 < nchunks) load_q(c + 1);   // Q rows are no longer read
 
     // ---- R = beta (v - e^gamma nk X) -> hi / lo tiles (K rows), those TMEM rows cleared;
     // Q rows: QS *= e^gamma nq in TMEM (fp32)
@@ -589,7 +599,7 @@ __global__ void __launch_bounds__(kChainThreads, 2) chunk_chain_kernel(
     if (tid == 0) wait_load(3);                        // the [T; M2] tile of chunk c
     sync_for_mma();
     if (sm.abort) { ok = false; break; }
-    if (tid == 0 && c + 1 < nchunks) load_v(c + 1);   // the v tile is consumed
+    if (tid == kLoader && c + 1 < nchunks) load_v(c + 1);   // the v tile is consumed
 
     // ---- (4) W-region += [T;M2] [R_hi;R_lo] : T rows -> v', M2 rows -> out
     if (tid == 0) {
@@ -650,7 +660,7 @@ __global__ void __launch_bounds__(kChainThreads, 2) chunk_chain_kernel(
       }
     }
     if (!(ok = wait_mma())) break;
-    if (tid == 0 && c + 1 < nchunks) load_k(c + 1);   // the K rows are free
+    if (tid == kLoader && c + 1 < nchunks) load_k(c + 1);   // the K rows are free
   }
   if (!ok && tid == 0) {   // drain loads still in flight before the CTA exits (bounded)
 #pragma unroll

@@ -220,6 +220,12 @@ __device__ __forceinline__ void bulk_commit() {
 __device__ __forceinline__ void bulk_wait_all() {
   asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
 }
+// TMA: 2-D tiled prefetch of a box into L2 (no shared memory, no completion).
+__device__ __forceinline__ void tma_prefetch_2d(const void* tmap, int x, int y) {
+  asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global [%0, {%1, %2}];" ::"l"(tmap), "r"(x),
+               "r"(y)
+               : "memory");
+}
 // 1-D bulk copy global -> shared (16-byte aligned addresses, size a multiple of
 // 16), completing on an mbarrier (transaction bytes).  No cluster multicast.
 __device__ __forceinline__ void bulk_load(uint32_t dst_smem, const void* src, uint32_t bytes,
