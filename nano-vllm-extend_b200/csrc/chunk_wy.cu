@@ -3,25 +3,30 @@
 // serial chain per (sequence, v-head) keeps only the state-dependent steps.
 //
 //   chunk_index_kernel  chunk_start[r] = sum over earlier sequences of
-//                       ceil(len / 64) (the workspace's block numbering)
+//                       ceil(len / 64) (the workspace's block numbering) and
+//                       chunk_info[b] = {first row, valid rows} of block b
 //   chunk_prep_kernel   one CTA (two warpgroups, three per SM) per (chunk, pair
 //                       of v-heads): P = [K;Q] K^T on the tensor core (once per
-//                       k-head), the l2 norms, the
-//                       decays, L and QKm, T = (I - L)^-1 (fp32), M2 = QKm T;
-//                       writes one 17,664-byte block: the [T; M2] tile as the
-//                       128B-swizzled shared-memory image MMA 4 reads, and the
-//                       per-token factors the chain applies
+//                       k-head), the l2 norms, the decays, L and QKm,
+//                       T = (I - L)^-1 (fp32; doubling products on tf32 mma
+//                       tiles), M2 = QKm T; writes one 17,664-byte block per
+//                       (chunk, head): the [T; M2] tile as the 128B-swizzled
+//                       shared-memory image MMA 4 reads, and the per-token
+//                       factors the chain applies
 //   chunk_chain_kernel  one CTA (256 threads, two per SM) per chain, longest
 //                       first; the fp32 state in TMEM; per chunk three M = 128
 //                       MMAs (XQ = [K;Q] S, [v'; out] += [T;M2] [R_hi;R_lo],
 //                       S += K^T [W_hi;W_lo]) and the CUDA-core phases between
 //                       them, split over 8 warps (warp w: TMEM lanes of quarter
-//                       w % 4, columns of half w / 4)
+//                       w % 4, columns of half w / 4; operand rows interleaved,
+//                       ilv_row); the output tile leaves by TMA from the
+//                       consumed [T; M2] buffer while MMA 5 runs
 //
-// The arithmetic is the single-kernel form's (chunk_tc.cu) step for step —
-// same operands, same roundings — so both give the same bits; the split only
-// changes where each step runs.  Blocks move by bulk copies (one store per
-// prep CTA, one load per chain chunk).  Every wait is bounded (status bit, TMEM freed, return).
+// The arithmetic is the one-kernel form's (chunk_tc.cu) step for step — same
+// operands, same roundings, shared code in chunk_common.cuh — so both give the
+// same bits; the split only changes where each step runs.  Blocks move by bulk
+// copies (one store per prep head, one load per chain chunk).  Every wait is
+// bounded (status bit, TMEM freed, return).
 #include "chunk_common.cuh"
 
 namespace gdn {
@@ -326,7 +331,7 @@ __global__ void __launch_bounds__(kPrepThreads, kPrepCtasPerSm) chunk_prep_kerne
 struct __align__(1024) ChainSmem {
   uint8_t kq[2][128 * 128];   // [dk block][row][128 B]: K / Q rows interleaved (ilv_row)
   uint8_t scratch[32768];     // the bf16 S tile for MMA 3, then R, then W (hi / lo)
-  uint8_t a4[128 * 128];      // [T ; M2] from the chunk's block
+  uint8_t a4[128 * 128];      // [T ; M2] from the chunk's block, then the out tile
   uint8_t v[2][64 * 128];     // [dv block][token row][128 B]
   float f[2][5][kC];          // the blocks' per-token factors, chunks c and c + 1
   unsigned long long mbar;    // MMA completion
