@@ -1,15 +1,19 @@
 // (c) Chunked gated-delta-rule prefill on tcgen05 tensor cores (sm_100a).
 //
-// One CTA (128 threads, thread t <-> TMEM lane t; two CTAs per SM) walks one
-// (sequence, v-head) chain chunk by chunk (64 tokens), the chains launched
-// longest first.  The fp32 state S [dk x dv] lives in TMEM for the whole
-// sequence: read from the pool slot at the start, written back at the end.  With q^ = l2norm(q)*scale, k^ = l2norm(k),
-// gamma = in-chunk cumsum(g) (qwen3_5.py:152-227), every chunk runs five
-// M = 128 MMAs (bf16 operands from 128B-swizzled shared memory, fp32
+// The one-kernel form, run when the caller passes no workspace (the split form
+// in chunk_wy.cu gives the same bits).  One CTA (128 threads, thread t <->
+// TMEM lane t; two CTAs per SM) walks one (sequence, v-head) chain chunk by
+// chunk (64 tokens), the chains launched longest first.  The fp32 state
+// S [dk x dv] lives in TMEM for the whole sequence: read from the pool slot at
+// the start, written back at the end.  With q^ = l2norm(q)*scale,
+// k^ = l2norm(k), gamma = in-chunk cumsum(g) (qwen3_5.py:152-227), every chunk
+// runs five M = 128 MMAs (bf16 operands from 128B-swizzled shared memory, fp32
 // accumulators in TMEM):
 //
 //   1. P   = [K;Q] [K;Q]^T             raw bf16 rows: exact products; its
-//                                      diagonal gives the row norms, and the
+//                                      diagonal gives the k norms (the q
+//                                      norms are summed on the CUDA cores),
+//                                      and the
 //                                      norms and decays are applied in fp32
 //                                      to build
 //        L   = -(beta_i nk_i nk_j P_ij e^(gamma_i - gamma_j))   (j < i)

@@ -745,7 +745,8 @@ int chunk_prefill_wy(int n_seqs, int HV, cudaStream_t s, const bf16* q, int64_t 
       tm_q, tm_k, g, beta, chunk_info, HK, HV, scale, blocks, status);
   if ((rc = check_launch("gdn_chunk_prefill_varlen")) != GDN_OK) return rc;
   wy::chunk_chain_kernel<<<(unsigned)((int64_t)n_seqs * HV), wy::kChainThreads, chain_smem, s>>>(
-      tm_q32, tm_k32, tm_v, tm_out, blocks, chunk_start, pool, slot_stride, num_slots, ids, cu, n_tokens,
+      tm_q32, tm_k32, tm_v, tm_out, blocks, chunk_start, pool, slot_stride, num_slots, ids, cu,
+      n_tokens,
       max_seqlen, out, HK, HV, status);
   return check_launch("gdn_chunk_prefill_varlen");
 }
