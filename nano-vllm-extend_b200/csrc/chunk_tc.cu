@@ -12,13 +12,13 @@
 //
 //   1. P   = [K;Q] [K;Q]^T             raw bf16 rows: exact products; its
 //                                      diagonal gives the k norms (the q
-//                                      norms are summed on the CUDA cores),
-//                                      and the
-//                                      norms and decays are applied in fp32
-//                                      to build
+//                                      norms are summed on the CUDA cores);
+//                                      norms and decays applied in fp32
+//                                      build
 //        L   = -(beta_i nk_i nk_j P_ij e^(gamma_i - gamma_j))   (j < i)
 //        QKm =  (nq_i nk_j QK_ij e^(gamma_i - gamma_j))          (j <= i)
-//      T = (I - L)^-1 by forward substitution on CUDA cores (fp32)
+//      T = (I - L)^-1 in fp32: diagonal blocks by forward substitution,
+//      the doubling products on tf32 mma tiles (chunk_common.cuh)
 //   2. M2  = QKm T                     (S-independent)
 //   3. XQ  = [K;Q] S_bf16              X = K S (rows 0-63), QS (rows 64-127)
 //      R   = beta (v - e^gamma nk X)   split into bf16 hi + lo
