@@ -92,23 +92,27 @@ __device__ __forceinline__ void k_norm_from_diag(ChunkScalars& s, uint32_t tl, u
   s.nk[tid] = n;
   s.cf[tid] = n * s.bcol[tid];
 }
-// Q rows (t >= 64): nq = scale/|q| summed on the CUDA cores in a fixed order
-// (rows past the sequence end count as zero rows).
-__device__ __forceinline__ void q_norm(ChunkScalars& s, const uint8_t* kq, int tid, int nv,
-                                       float scale) {
-  const int i = tid - 64;
+// Q row of token i at tile row `row`: nq = scale/|q| summed on the CUDA cores in
+// a fixed order (rows past the sequence end count as zero rows).
+__device__ __forceinline__ void q_norm_row(ChunkScalars& s, const uint8_t* kq, int i, int row,
+                                           int nv, float scale) {
   float a0 = 0.f, a1 = 0.f;
   if (i < nv) {
 #pragma unroll
     for (int c = 0; c < 16; ++c) {
       float f[8];
-      unpack8(*reinterpret_cast<const uint4*>(kq + (c >> 3) * 16384 + sw128(64 + i, (c & 7) * 8)),
+      unpack8(*reinterpret_cast<const uint4*>(kq + (c >> 3) * 16384 + sw128(row, (c & 7) * 8)),
               f);
 #pragma unroll
       for (int e = 0; e < 8; e += 2) ffma2(a0, a1, f[e], f[e + 1], f[e], f[e + 1], a0, a1);
     }
   }
   s.nq[i] = rsqrtf(a0 + a1 + 1e-6f) * scale;
+}
+// Q rows (t >= 64) of the [K;Q] tile.
+__device__ __forceinline__ void q_norm(ChunkScalars& s, const uint8_t* kq, int tid, int nv,
+                                       float scale) {
+  q_norm_row(s, kq, tid - 64, tid, nv, scale);
 }
 
 // From P (TMEM, thread t <-> lane t of 128): rows 0-63 build
@@ -169,6 +173,88 @@ __device__ __forceinline__ void build_l_qkm(const ChunkScalars& s, uint32_t tl, 
       for (int q4 = 0; q4 < 8; ++q4)
         *reinterpret_cast<float4*>(&Lm[i][hh * 32 + q4 * 4]) =
             make_float4(p[4 * q4], p[4 * q4 + 1], p[4 * q4 + 2], p[4 * q4 + 3]);
+    }
+  }
+}
+
+// A [K;Q] tile interleaved by 16 rows, [K 0-15; Q 0-15; K 16-31; Q 16-31; ...]:
+// tile row of token i's K row (second = false) or Q row (second = true).  With
+// P = [K;Q][K;Q]^T in TMEM, warp w (lane quarter w % 4) then holds the K and Q
+// rows of one 16-token block, so the block-structured L / QKm build below runs
+// without divergence between the two blocks a plain [K;Q] quarter would mix.
+__host__ __device__ constexpr int ilv16_row(int i, bool second) {
+  return 32 * (i >> 4) + (i & 15) + (second ? 16 : 0);
+}
+
+// nk = 1/|k| from P's diagonal for the interleaved tile: lanes 0-15 of each
+// warp (K rows of block w % 4); all 32 lanes load (warp-collective).
+__device__ __forceinline__ void k_norm_ilv16(ChunkScalars& s, uint32_t tl, uint32_t colP,
+                                             int tid) {
+  const int q = (tid >> 5) & 3, lane = tid & 31;
+  float p[32];
+  tmem_ld32(tl + colP + q * 32, p);
+  float d = 0.f;
+#pragma unroll
+  for (int jj = 0; jj < 32; ++jj) d = (jj == lane) ? p[jj] : d;
+  if (lane < 16) {
+    const int i = 16 * q + lane;
+    const float n = rsqrtf(d + 1e-6f);
+    s.nk[i] = n;
+    s.cf[i] = n * s.bcol[i];
+  }
+}
+
+// L (K rows) and QKm (Q rows) from P for the interleaved tile — the arithmetic of
+// build_l_qkm, with the row's 16-token block uniform across the warp.  K token
+// j's column is ilv16_row(j, false).
+__device__ __forceinline__ void build_l_qkm_ilv16(const ChunkScalars& s, uint32_t tl,
+                                                  uint32_t colP, int tid, float (*Lm)[kLP],
+                                                  uint8_t* qkm) {
+  const int I = (tid >> 5) & 3, lane = tid & 31;
+  const bool isq = lane >= 16;
+  const int i = 16 * I + (lane & 15);
+  const float gi = s.gam[i];
+  const float rowf = isq ? s.nq[i] : -s.bet[i] * s.nk[i];
+#pragma unroll 1   // rolled: code size (instruction-cache pressure)
+  for (int J = 0; J < 4; ++J) {
+    float pe[16];
+    tmem_ld16(tl + colP + 32 * J, pe);
+    if (J < I) {                       // warp-uniform
+      const float rf = rowf * __expf(gi - s.gend[J]);
+#pragma unroll
+      for (int jj = 0; jj < 16; jj += 4) {
+        const float4 c4 = *reinterpret_cast<const float4*>(&s.cf[J * 16 + jj]);
+        float f0, f1, f2, f3;
+        fmul2(f0, f1, rf, rf, c4.x, c4.y);
+        fmul2(f2, f3, rf, rf, c4.z, c4.w);
+        fmul2(pe[jj], pe[jj + 1], pe[jj], pe[jj + 1], f0, f1);
+        fmul2(pe[jj + 2], pe[jj + 3], pe[jj + 2], pe[jj + 3], f2, f3);
+      }
+    } else if (J == I) {
+#pragma unroll
+      for (int j4 = 0; j4 < 16; j4 += 4) {
+        const float4 n4 = *reinterpret_cast<const float4*>(&s.nk[J * 16 + j4]);
+        const float4 g4 = *reinterpret_cast<const float4*>(&s.gam[J * 16 + j4]);
+        const float nv4[4] = {n4.x, n4.y, n4.z, n4.w}, gv4[4] = {g4.x, g4.y, g4.z, g4.w};
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const int jj = j4 + k, j = J * 16 + jj;
+          const bool keep = isq ? (j <= i) : (j < i);
+          pe[jj] = keep ? pe[jj] * rowf * nv4[k] * __expf(gi - gv4[k]) : 0.f;
+        }
+      }
+    } else {
+#pragma unroll
+      for (int jj = 0; jj < 16; ++jj) pe[jj] = 0.f;
+    }
+    if (isq) {
+      st8(qkm, i, J * 16, pe);
+      st8(qkm, i, J * 16 + 8, pe + 8);
+    } else {
+#pragma unroll
+      for (int q4 = 0; q4 < 4; ++q4)
+        *reinterpret_cast<float4*>(&Lm[i][J * 16 + q4 * 4]) =
+            make_float4(pe[4 * q4], pe[4 * q4 + 1], pe[4 * q4 + 2], pe[4 * q4 + 3]);
     }
   }
 }

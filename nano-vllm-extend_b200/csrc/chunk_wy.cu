@@ -119,9 +119,10 @@ __global__ void __launch_bounds__(kIndexThreads) chunk_index_kernel(
 // warpgroup w handles v-head 2p + w.  When the two heads share a k-head (GQA),
 // the [K;Q] tile, P = [K;Q] K^T and the l2 norms are made once for both; else
 // each warpgroup loads its own tile.  Each warpgroup's 32 KiB region serves in
-// turn as its [K;Q] tile, as L / T (fp32), the QKm tile and X (the inverse),
-// and as its [T; M2] block image (MMA 2 and the store) — about 71 KiB and 128
-// TMEM columns per CTA: three CTAs (six heads) per SM.
+// turn as its [K;Q] tile (rows interleaved by 16, ilv16_row), as L / T (fp32),
+// the QKm tile and X (the inverse), and as its [T; M2] block image (MMA 2 and
+// the store) — about 71 KiB and 128 TMEM columns per CTA (256 when the two
+// heads have their own k-heads): three CTAs (six heads) per SM.
 struct PrepSmem {             // placed at a 1024-byte aligned base (swizzle atoms)
   uint8_t r[2][32768];
   float f[2][5][kC];          // the blocks' factors
@@ -167,15 +168,7 @@ __global__ void __launch_bounds__(kPrepThreads, kPrepCtasPerSm) chunk_prep_kerne
     mbar_init(lbar, 1);
     mbar_init_fence();
     sm.abort = 0;
-    mbar_expect_tx(lbar, (own1 ? 2 : 1) * 4 * 8192);
-    for (int blk = 0; blk < 2; ++blk) {
-      tma_load_2d(r0s + blk * 16384, &tm_k, hk0 * kD + blk * 64, (int)t0, lbar);
-      tma_load_2d(r0s + blk * 16384 + 64 * 128, &tm_q, hk0 * kD + blk * 64, (int)t0, lbar);
-      if (own1) {
-        tma_load_2d(r1s + blk * 16384, &tm_k, hk1 * kD + blk * 64, (int)t0, lbar);
-        tma_load_2d(r1s + blk * 16384 + 64 * 128, &tm_q, hk1 * kD + blk * 64, (int)t0, lbar);
-      }
-    }
+    mbar_expect_tx(lbar, (own1 ? 2 : 1) * 4 * 8192);   // the boxes are issued after the barrier
   }
   if (lt < kC) {
     float gv = 0.f, bv = 0.f;
@@ -186,13 +179,25 @@ __global__ void __launch_bounds__(kPrepThreads, kPrepCtasPerSm) chunk_prep_kerne
     sm.sc[wg].gam[lt] = gv;
     sm.sc[wg].bet[lt] = bv;
   }
-  if (warp == 0) tmem_alloc(smem_u32(&sm.tmem_base), 128);
+  const uint32_t tcols = own1 ? 256u : 128u;          // P (128 columns) per k-head
+  if (warp == 0) tmem_alloc(smem_u32(&sm.tmem_base), tcols);
   fence_before();
   __syncthreads();
   fence_after();
+  if (lane == 0) {   // 16-row boxes at their interleaved tile rows: warp w -> (dk block, block)
+    const int blk = warp & 1, b16 = warp >> 1;
+    for (int t = 0; t < (own1 ? 2 : 1); ++t) {
+      const uint32_t rs = (t ? r1s : r0s) + blk * 16384;
+      const int hk = t ? hk1 : hk0;
+      tma_load_2d(rs + ilv16_row(16 * b16, false) * 128, &tm_k, hk * kD + blk * 64,
+                  (int)(t0 + 16 * b16), lbar);
+      tma_load_2d(rs + ilv16_row(16 * b16, true) * 128, &tm_q, hk * kD + blk * 64,
+                  (int)(t0 + 16 * b16), lbar);
+    }
+  }
   const uint32_t tbase = sm.tmem_base;
   const uint32_t tl = tbase + ((uint32_t)((warp & 3) * 32) << 16);   // lane quarter warp % 4
-  const uint32_t colP = own1 ? 64u * wg : 0u;        // this head's P columns
+  const uint32_t colP = own1 ? 128u * wg : 0u;       // this head's P columns
   // one thread waits on each barrier; the others wait at the CTA barrier
   auto wait1 = [&](uint32_t mb, uint32_t ph) -> bool {
     if (tid == 0 && !mbar_wait(mb, ph, kSpin)) {
@@ -211,8 +216,8 @@ __global__ void __launch_bounds__(kPrepThreads, kPrepCtasPerSm) chunk_prep_kerne
         const int t = idx / ((kC - nv) * 16), rem = idx - t * (kC - nv) * 16;
         const int i = nv + rem / 16, ch = rem % 16, blk = ch >> 3, c8 = (ch & 7) * 8;
         const uint4 z = make_uint4(0, 0, 0, 0);
-        *reinterpret_cast<uint4*>(sm.r[t] + blk * 16384 + sw128(i, c8)) = z;
-        *reinterpret_cast<uint4*>(sm.r[t] + blk * 16384 + sw128(64 + i, c8)) = z;
+        *reinterpret_cast<uint4*>(sm.r[t] + blk * 16384 + sw128(ilv16_row(i, false), c8)) = z;
+        *reinterpret_cast<uint4*>(sm.r[t] + blk * 16384 + sw128(ilv16_row(i, true), c8)) = z;
       }
     }
     if ((warp & 3) == 0) decay_scan(sm.sc[wg], lane);   // warps 0 and 4: one head each
@@ -220,7 +225,7 @@ __global__ void __launch_bounds__(kPrepThreads, kPrepCtasPerSm) chunk_prep_kerne
     fence_before();
     __syncthreads();
     fence_after();
-    // (1) P = [K;Q] K^T : M = 128, N = 64 (the K rows), K = 128; once per k-head
+    // (1) P = [K;Q] [K;Q]^T (interleaved rows) : M = N = K = 128; once per k-head
     if (tid == 0) {
 #pragma unroll
       for (int t = 0; t < 2; ++t) {
@@ -229,18 +234,18 @@ __global__ void __launch_bounds__(kPrepThreads, kPrepCtasPerSm) chunk_prep_kerne
 #pragma unroll
         for (int s = 0; s < 8; ++s) {
           const uint32_t off = (uint32_t)(s >> 2) * 16384u + (uint32_t)(s & 3) * 32u;
-          mma_bf16(tbase + 64u * t, smem_desc(rs + off, 16, 1024), smem_desc(rs + off, 16, 1024),
-                   idesc_bf16(128, 64, false, false), s > 0);
+          mma_bf16(tbase + 128u * t, smem_desc(rs + off, 16, 1024), smem_desc(rs + off, 16, 1024),
+                   idesc_bf16(128, 128, false, false), s > 0);
         }
       }
       mma_commit(bar);
     }
     if (lt >= 64 && (wg == 0 || own1))          // Q rows: CUDA cores, under MMA 1
-      q_norm(sm.sc[wg], rw, lt, nv, scale);
+      q_norm_row(sm.sc[wg], rw, lt - 64, ilv16_row(lt - 64, true), nv, scale);
     ok = wait1(bar, 0);
   }
   if (ok) {
-    if (lt < 64 && (wg == 0 || own1)) k_norm_from_diag(sm.sc[wg], tl, colP, lt);   // P's diagonal
+    if (wg == 0 || own1) k_norm_ilv16(sm.sc[wg], tl, colP, lt);   // P's diagonal (K rows)
     __syncthreads();
     if (wg == 1 && !own1) {                      // head 1 shares head 0's norms
       if (lt < 64) {
@@ -253,7 +258,7 @@ __global__ void __launch_bounds__(kPrepThreads, kPrepCtasPerSm) chunk_prep_kerne
     __syncthreads();
     float (*Lm)[kLP] = reinterpret_cast<float (*)[kLP]>(rw);     // K / Q are consumed
     float* Xs = reinterpret_cast<float*>(rw + kXOff);
-    build_l_qkm(sm.sc[wg], tl, colP, lt, Lm, rw + kQkmOff);
+    build_l_qkm_ilv16(sm.sc[wg], tl, colP, lt, Lm, rw + kQkmOff);
     __syncthreads();
     invert_unit_lower(Lm, Xs, lt);               // both warpgroups pass its barriers together
     {   // T (fp32, rows of 68) -> the bf16 T rows of the block image, over L / T
@@ -324,7 +329,7 @@ __global__ void __launch_bounds__(kPrepThreads, kPrepCtasPerSm) chunk_prep_kerne
   fence_before();
   __syncthreads();
   fence_after();
-  if (warp == 0) tmem_dealloc(tbase, 128);
+  if (warp == 0) tmem_dealloc(tbase, tcols);
 }
 
 // ---------------------------------------------------------------- chain
@@ -711,9 +716,9 @@ int chunk_prefill_wy(int n_seqs, int HV, cudaStream_t s, const bf16* q, int64_t 
                      const int64_t* ids, const int32_t* cu, int64_t n_tokens, int max_seqlen,
                      bf16* out, int HK, float scale, void* workspace, int32_t* status) {
   using namespace tc;
-  CUtensorMap tm_q, tm_k, tm_v, tm_q32, tm_k32, tm_out;
-  if (!make_tile_map(&tm_q, q, (int64_t)HK * kD, n_tokens, qs) ||
-      !make_tile_map(&tm_k, k, (int64_t)HK * kD, n_tokens, ks) ||
+  CUtensorMap tm_q, tm_k, tm_v, tm_q32, tm_k32, tm_out;   // tm_q / tm_k: 16-row boxes (prep)
+  if (!make_tile_map(&tm_q, q, (int64_t)HK * kD, n_tokens, qs, 16) ||
+      !make_tile_map(&tm_k, k, (int64_t)HK * kD, n_tokens, ks, 16) ||
       !make_tile_map(&tm_q32, q, (int64_t)HK * kD, n_tokens, qs, 32) ||
       !make_tile_map(&tm_k32, k, (int64_t)HK * kD, n_tokens, ks, 32) ||
       !make_tile_map(&tm_v, v, (int64_t)HV * kD, n_tokens, vs) ||
