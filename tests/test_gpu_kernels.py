@@ -301,6 +301,8 @@ def test_chunk_split_equals_one_shot(ops):
     ([300, 5], 4, 4),                                 # one v-head per k-head
     ([129], 1, 4),                                    # four v-heads per k-head
     (list(I.rng(33).integers(0, 150, 300)), 1, 2),    # > 256 sequences: launch-order chains
+    ([100, 64, 7], 1, 3),                             # odd v-head count: a half-empty last pair
+    ([129, 40], 2, 6),                                # three v-heads per k-head: a pair across two
 ])
 def test_chunk_split_form_equals_one_kernel_form(ops, lens, HK, HV):
     """Head dim 128: the split form (per-chunk prep pass + chain) and the
