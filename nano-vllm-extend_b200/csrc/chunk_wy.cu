@@ -48,9 +48,9 @@ constexpr int kIndexThreads = 1024;
 // The chain's 128-row MMA operands interleave their two 64-row halves by 32
 // rows: tile rows [first 0-31; second 0-31; first 32-63; second 32-63] for
 // [K;Q] and [T;M2].  An MMA output row lands in the TMEM lane of its operand
-// row, and warp w (issuing on SM sub-partition w % 4) reaches lanes of
-// quarter w % 4 only, so each sub-partition then holds one quarter of the
-// heavy rows (R, W: the first half) and one of the light ones (QS, out).
+// row, and warp w reaches lanes of quarter w % 4 only, so quarters 0 and 2 hold
+// the K / T rows (R and W phases) and quarters 1 and 3 the Q / M2 rows (QS
+// scaling, output).
 __host__ __device__ constexpr int ilv_row(int token, bool second) {
   return token + (token & 32) + (second ? 32 : 0);
 }
