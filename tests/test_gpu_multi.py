@@ -54,3 +54,16 @@ def test_tp2_head_sharded_layer_nccl(D):
 def test_pipeline_handoff_nccl(mode):
     _need(2)
     assert _run(W.nccl_handoff_worker, mode) == [0, 0]
+
+
+@pytest.mark.parametrize("D", [128, 64])
+def test_tp4_head_sharded_layer_nccl(D):
+    """Four TP ranks: one k-head and two v-heads each."""
+    _need(4)
+    assert _run(W.tp_layer_worker, D, world=4) == [0, 0, 0, 0]
+
+
+@pytest.mark.parametrize("mode", ["packed", "presum"])
+def test_pipeline_handoff_nccl_4_stages(mode):
+    _need(4)
+    assert _run(W.nccl_handoff_worker, mode, world=4) == [0, 0, 0, 0]
