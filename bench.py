@@ -33,6 +33,7 @@ import os
 import statistics
 import subprocess
 import sys
+import tempfile
 import time
 
 import numpy as np
@@ -106,15 +107,15 @@ class Clocks:
     def __init__(self, index: int):
         self.index = index
         self.proc = None
-        self.path = os.path.join(ROOT, "gpurun_out", f".clocks_{os.getpid()}.csv")
+        fd, self.path = tempfile.mkstemp(prefix="gdn_clocks_", suffix=".csv")
+        os.close(fd)
 
     def start(self):
         try:
-            os.makedirs(os.path.dirname(self.path), exist_ok=True)
             self.f = open(self.path, "w")
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}",
-                 "--format=csv,noheader,nounits", "-lms", "50"], stdout=self.f,
+                 "--format=csv,noheader,nounits", "-lms", "20"], stdout=self.f,
                 stderr=subprocess.DEVNULL)
         except Exception:
             self.proc = None
@@ -525,14 +526,17 @@ def prefill_bench(pkg, device, steps, peaks):
 # ---------------------------------------------------------------------------
 
 
-def cpu_layer_step_sampler(seed=0):
-    """One config-1 layer decode step on the host: numpy projections (BLAS),
-    gate / conv / norm in numpy, the recurrence in the C restatement over a
-    257-slot pool.  Returns (callable, sample description, threads)."""
+def cpu_decode_stack(seed=0):
+    """The config-1 decode step on the host cores: all 18 GDN layers, each with
+    its own 257-slot state and conv pools (256 sequences + 1), numpy BLAS
+    projections, gate / conv / norm in numpy, the recurrence in the C
+    restatement; residual add between layers.  Returns (step callable,
+    sample description, threads)."""
     from oracle import cref
     from oracle import gdn_oracle as O
+    threads = cref.use_all_cores()
     c = C1
-    bs, H, HK, HV, D = c["bs"], c["hidden"], c["HK"], c["HV"], c["DK"]
+    L, bs, H, HK, HV, D = c["layers"], c["bs"], c["hidden"], c["HK"], c["HV"], c["DK"]
     cd = 2 * HK * D + HV * D
     r = np.random.Generator(np.random.PCG64(seed))
     Wf = (r.standard_normal((cd + HV * D + 2 * HV, H), dtype=np.float32) * H ** -0.5)
@@ -541,12 +545,17 @@ def cpu_layer_step_sampler(seed=0):
     a_log = r.uniform(-1, 0, HV).astype(np.float32)
     dt_bias = np.zeros(HV, np.float32)
     norm_w = np.ones(D, np.float32)
-    pool = (r.standard_normal((bs + 1, HV, D, D), dtype=np.float32) * 0.02)
-    conv_pool = r.standard_normal((bs + 1, cd, c["K"] - 1), dtype=np.float32)
+    # per-layer pools; the states of the first layer are N(0, 0.02), copied to the others
+    pools = np.empty((L, bs + 1, HV, D, D), np.float32)
+    pools[0] = r.standard_normal((bs + 1, HV, D, D), dtype=np.float32) * 0.02
+    for i in range(1, L):
+        pools[i] = pools[0]
+    conv_pools = np.empty((L, bs + 1, cd, c["K"] - 1), np.float32)
+    conv_pools[:] = r.standard_normal((bs + 1, cd, c["K"] - 1), dtype=np.float32)
     ids = r.permutation(bs + 1)[:bs]
-    x = r.standard_normal((bs, H), dtype=np.float32)
+    x0 = r.standard_normal((bs, H), dtype=np.float32)
 
-    def step():
+    def layer(x, pool, conv_pool):
         p = x @ Wf.T
         mixed, z = p[:, :cd], p[:, cd:cd + HV * D]
         b, a = p[:, cd + HV * D:cd + HV * D + HV], p[:, cd + HV * D + HV:]
@@ -554,7 +563,8 @@ def cpu_layer_step_sampler(seed=0):
         # conv step (vectorised restatement of qwen3_5.py:515-558)
         st = conv_pool[ids]
         acc = mixed * conv_w[:, 3] + (st * conv_w[None, :, :3]).sum(-1)
-        y = acc / (1 + np.exp(-acc))
+        with np.errstate(over="ignore"):   # silu of a large negative input is 0
+            y = acc / (1 + np.exp(-acc))
         conv_pool[ids] = np.concatenate([st[:, :, 1:], mixed[:, :, None]], -1)
         q = y[:, :HK * D].reshape(bs, HK, D)
         k = y[:, HK * D:2 * HK * D].reshape(bs, HK, D)
@@ -563,9 +573,16 @@ def cpu_layer_step_sampler(seed=0):
         core = O.rms_norm_gated(o, z.reshape(bs, HV, D), norm_w, 1e-6, None)
         return core.reshape(bs, HV * D) @ Wo.T
 
-    sample = ("1 of 18 config-1 GDN layers per step (bs 256, 257-slot pool), numpy BLAS "
-              "projections + C/OpenMP recurrence, scaled x18 for the 18-layer step")
-    return step, sample, cref.num_threads()
+    def step():
+        h = x0
+        for i in range(L):
+            h = h + layer(h, pools[i], conv_pools[i])
+        return h
+
+    sample = (f"the whole config-1 step per step: {L} GDN layers, bs {bs}, each layer's "
+              f"state in its own {bs + 1}-slot pool (256 sequences + 1), numpy BLAS "
+              "projections + C/OpenMP recurrence")
+    return step, sample, threads
 
 
 def cpu_prefill_baseline(budget_s=8.0):
@@ -574,6 +591,7 @@ def cpu_prefill_baseline(budget_s=8.0):
     budget allows, extrapolated per token.  Projections, conv and norm are not
     included (the GPU chunk-kernel figure excludes them too)."""
     from oracle import cref
+    cref.use_all_cores()
     c = C2
     HK, HV, D, T = c["HK"], c["HV"], c["DK"], 512
     r = np.random.Generator(np.random.PCG64(5))
@@ -598,47 +616,62 @@ def cpu_prefill_baseline(budget_s=8.0):
                       "(head dim 128, chunk 64) in the C/OpenMP restatement, per token"}
 
 
-def cpu_baseline(budget_s=12.0):
-    step, sample, threads = cpu_layer_step_sampler()
+def cpu_baseline(budget_s=20.0):
+    """The CPU decode stack on a bounded number of whole steps (~budget_s)."""
+    step, sample, threads = cpu_decode_stack()
     step()
     n, t0 = 0, time.perf_counter()
     while True:
         step()
         n += 1
-        if time.perf_counter() - t0 > budget_s or n >= 20:
+        if time.perf_counter() - t0 > budget_s:
             break
-    per_layer = (time.perf_counter() - t0) / n
-    tok_s = C1["bs"] / (per_layer * C1["layers"])
-    return {"value": round(tok_s, 2), "unit": "tok/s", "cores": threads, "kind": "port",
-            "sample": f"{sample}; {n} layer-steps timed", "ms_per_layer_step": round(per_layer * 1e3, 2)}
+    dt = (time.perf_counter() - t0) / n
+    return {"value": round(C1["bs"] / dt, 2), "unit": "tok/s", "cores": threads, "kind": "port",
+            "sample": f"{sample}; {n} whole steps timed", "ms_per_step": round(dt * 1e3, 1)}
+
+
+def decode_config(world):
+    """The config dict of the decode line (both arms print the same one)."""
+    c = C1
+    return {"workload": "config1 GDN decode stack", "layers": c["layers"],
+            "global_batch": c["bs"] * world, "per_gpu_batch": c["bs"],
+            "hidden": c["hidden"], "qk_heads": c["HK"], "v_heads": c["HV"],
+            "head_dim": c["DK"], "conv_kernel": c["K"], "pool_slots": c["slots"],
+            "state_dtype": "fp32", "l2": "inputs larger than L2 (38.7 GB state pool)",
+            "cuda_graph": True, "parallelism": f"dp{world} (independent sequences)"}
+
+
+DECODE_METRIC = "GDN decode tok/s (config 1: 18-layer stack, bs 256)"
 
 
 def run_reference(args, world, rank):
+    """The reference arm: the CPU restatement of the path on the host cores,
+    whole 18-layer steps (rank 0 only; other ranks exit without work).  The
+    timed step count is capped so the run stays within about a minute."""
     if rank != 0:
         return
-    import torch as _t  # noqa: F401  (BLAS threads)
-    step, sample, threads = cpu_layer_step_sampler()
-    step()
-    for _ in range(max(0, args.warmup - 1)):
-        step()
-    steps = max(1, args.steps)
-    # bounded: each "step" is one layer of the 18-layer step, scaled
+    step, sample, threads = cpu_decode_stack()
     t0 = time.perf_counter()
-    for _ in range(min(steps, 20)):
+    step()
+    est = time.perf_counter() - t0
+    for _ in range(min(max(0, args.warmup - 1), 2)):
         step()
-    n = min(steps, 20)
-    per_layer = (time.perf_counter() - t0) / n
-    ms_step = per_layer * C1["layers"] * 1e3
-    tok_s = C1["bs"] / (ms_step / 1e3)
-    line = {"metric": "GDN decode tok/s (config 1: 18-layer stack, bs 256)", "impl": "reference",
+    n = max(1, min(args.steps, int(45.0 / max(est, 1e-3))))
+    t0 = time.perf_counter()
+    for _ in range(n):
+        step()
+    dt = (time.perf_counter() - t0) / n
+    tok_s = C1["bs"] / dt
+    line = {"metric": DECODE_METRIC, "impl": "reference",
             "value": round(tok_s, 2), "unit": "tok/s", "n_gpus": args.gpus, "steps": n,
-            "warmup": args.warmup, "ms_per_step": round(ms_step, 2), "higher_is_better": True,
+            "warmup": args.warmup, "ms_per_step": round(dt * 1e3, 2), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": {"workload": "config1 GDN decode stack (CPU restatement, sampled)",
-                       "layers": 18, "global_batch": 256, "hidden": 2048, "qk_heads": 16,
-                       "v_heads": 32, "head_dim": 128, "pool_slots": 1024},
+            "config": decode_config(world),
             "cpu_baseline": {"value": round(tok_s, 2), "unit": "tok/s", "cores": threads,
-                             "kind": "port", "sample": f"{sample}; {n} layer-steps timed"},
+                             "kind": "port",
+                             "sample": f"{sample}; {n} whole steps timed (of {args.steps} "
+                                       f"asked), warm-up capped at 3"},
             "e2e": {"value": round(tok_s, 2), "unit": "tok/s", "h2d_bytes_per_step": 0,
                     "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
@@ -771,17 +804,12 @@ def main():
     roof = decode_kernel_roofline(pkg, stack, peaks, launches=max(2, args.steps // 10))
     state_bytes_step = c["layers"] * 2 * c["bs"] * c["HV"] * c["DK"] * c["DV"] * 4
 
-    line = {"metric": "GDN decode tok/s (config 1: 18-layer stack, bs 256)",
+    line = {"metric": DECODE_METRIC,
             "value": round(value, 1), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(t / args.steps * 1e3, 4),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic (seeded random weights, inputs and states)",
-            "config": {"workload": "config1 GDN decode stack", "layers": c["layers"],
-                       "global_batch": c["bs"] * world, "per_gpu_batch": c["bs"],
-                       "hidden": c["hidden"], "qk_heads": c["HK"], "v_heads": c["HV"],
-                       "head_dim": c["DK"], "conv_kernel": c["K"], "pool_slots": c["slots"],
-                       "state_dtype": "fp32", "l2": "inputs larger than L2 (38.7 GB state pool)",
-                       "cuda_graph": True, "parallelism": f"dp{world} (independent sequences)"},
+            "config": decode_config(world),
             "state_gbs": round(world * state_bytes_step * args.steps / t / 1e9, 1),
             "e2e": e2e, "roofline": roof,
             # per layer: the fused decode core (1 launch), or gate, conv step and

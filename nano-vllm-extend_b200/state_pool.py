@@ -2,8 +2,9 @@
 kernels honour.
 
 Mirrors engine/model_runner.py:265-322 (pool layout, per-layer view binding,
-dummy slot, zero-on-fresh-prefill) and engine/linear_state_pool.py:12-27
-(the host free list):
+dummy slot, zero-on-fresh-prefill).  Slot ids themselves come from the
+engine's own free list (engine/linear_state_pool.py), which this package
+does not replace:
 
 * ``s_pool``    fp32 [num_slots + 1, L, HV, DK, DV]
 * ``conv_pool`` model dtype [num_slots + 1, L, conv_dim, K - 1]
@@ -18,28 +19,7 @@ run (16-byte aligned), which is what the decode kernel streams.
 """
 from __future__ import annotations
 
-from collections import deque
-
 import torch
-
-
-class LinearStatePool:
-    """Host-side free list of slot ids (engine/linear_state_pool.py:12-27)."""
-
-    def __init__(self, num_slots: int):
-        self.num_slots = num_slots
-        self.free_slots: deque[int] = deque(range(num_slots))
-
-    def alloc(self) -> int:
-        assert self.free_slots, "no free linear-state slots"
-        return self.free_slots.popleft()
-
-    def free(self, slot: int):
-        self.free_slots.append(slot)
-
-    @property
-    def num_free(self) -> int:
-        return len(self.free_slots)
 
 
 def gdn_modules(model: torch.nn.Module):

@@ -24,6 +24,8 @@ def load():
         lib = C.CDLL(LIB_PATH)
         vp, i64, i32, f32 = C.c_void_p, C.c_int64, C.c_int, C.c_float
         lib.gdn_ref_num_threads.restype = C.c_int
+        lib.gdn_ref_set_num_threads.argtypes = [C.c_int]
+        lib.gdn_ref_set_num_threads.restype = None
         lib.gdn_ref_recurrent_inplace.argtypes = [vp, i64, vp, i64, vp, i64, vp, vp, vp, i64, vp,
                                                   i32, i32, i32, i32, i32, f32, vp]
         lib.gdn_ref_chunk_prefill.argtypes = [vp, i64, vp, i64, vp, i64, vp, vp, vp, i64, vp, vp,
@@ -34,6 +36,19 @@ def load():
 
 def num_threads() -> int:
     return load().gdn_ref_num_threads()
+
+
+def use_all_cores() -> int:
+    """Run the C restatement and numpy's BLAS on every host core (torchrun
+    exports OMP_NUM_THREADS=1 to its workers); returns the thread count."""
+    n = os.cpu_count() or 1
+    load().gdn_ref_set_num_threads(n)
+    try:
+        import threadpoolctl
+        threadpoolctl.threadpool_limits(limits=n)
+    except Exception:   # BLAS thread control is best effort
+        pass
+    return num_threads()
 
 
 def _f32(a):

@@ -32,6 +32,15 @@ int gdn_ref_num_threads(void) {
 #endif
 }
 
+/* Use n threads in later calls (a launcher may have exported OMP_NUM_THREADS=1). */
+void gdn_ref_set_num_threads(int n) {
+#ifdef _OPENMP
+  if (n > 0) omp_set_num_threads(n);
+#else
+  (void)n;
+#endif
+}
+
 static void l2norm_scaled(const float* x, int n, float scale, float* out) {
   float s = 0.f;
   for (int i = 0; i < n; ++i) s += x[i] * x[i];
@@ -79,14 +88,18 @@ void gdn_ref_recurrent_inplace(const float* q, int64_t qs, const float* k, int64
 
 #define CH 64
 
-/* Chunked prefill of one (sequence, head) unit: T tokens starting at row t0. */
+/* Chunked prefill of one (sequence, head) unit: T tokens starting at row t0.
+ * Every matrix product keeps the reference's association (the decay factors
+ * are applied to an operand before the product, as the batched tensor ops of
+ * :201-222 do) and sums over the contracted index in increasing order; the
+ * loops run with the output column innermost so they vectorise. */
 static void chunk_unit(const float* q, int64_t qs, const float* k, int64_t ks, const float* v,
                        int64_t vs, const float* g, const float* beta, int64_t t0, int64_t T,
                        int h, int hk, int HV, int DK, int DV, float scale, float* S, float* out,
                        float* work) {
   float* Q = work;               /* [CH][DK] */
   float* K = Q + CH * DK;        /* [CH][DK] */
-  float* KB = K + CH * DK;       /* k_beta [CH][DK] */
+  float* KB = K + CH * DK;       /* k_beta [CH][DK], then k_beta * exp(g) */
   float* VB = KB + CH * DK;      /* v_beta [CH][DV] */
   float* U = VB + CH * DV;       /* value = attn @ v_beta [CH][DV] */
   float* W = U + CH * DV;        /* k_cumdecay [CH][DK] */
@@ -95,7 +108,9 @@ static void chunk_unit(const float* q, int64_t qs, const float* k, int64_t ks, c
   float* DM = A + CH * CH;       /* decay mask [CH][CH] */
   float* QK = DM + CH * CH;      /* [CH][CH] */
   float* SN = QK + CH * CH;      /* new state [DK][DV] */
-  float G[CH], B[CH];
+  float* KE = SN + DK * DV;      /* k * exp(g_last - g) [CH][DK] */
+  float* acc = KE + CH * DK;     /* one output row [max(DK, DV)] */
+  float G[CH], B[CH], EG[CH];
   const int64_t nch = (T + CH - 1) / CH;
   for (int64_t c = 0; c < nch; ++c) {
     const int64_t base = t0 + c * CH;
@@ -117,6 +132,7 @@ static void chunk_unit(const float* q, int64_t qs, const float* k, int64_t ks, c
       for (int j = 0; j < DK; ++j) KB[i * DK + j] = K[i * DK + j] * B[i];
     }
     for (int i = 1; i < CH; ++i) G[i] += G[i - 1]; /* cumsum (:193) */
+    for (int i = 0; i < CH; ++i) EG[i] = expf(G[i]);
     for (int i = 0; i < CH; ++i)
       for (int j = 0; j < CH; ++j) DM[i * CH + j] = j <= i ? expf(G[i] - G[j]) : 0.f;
     /* attn = -(k_beta k^T * decay), strictly lower (:195) */
@@ -139,16 +155,17 @@ static void chunk_unit(const float* q, int64_t qs, const float* k, int64_t ks, c
     }
     for (int i = 0; i < CH; ++i) A[i * CH + i] += 1.f;
     /* value = attn @ v_beta; k_cumdecay = attn @ (k_beta * exp(g)) (:201-202) */
+    for (int m = 0; m < CH; ++m)
+      for (int j = 0; j < DK; ++j) KB[m * DK + j] *= EG[m];
     for (int i = 0; i < CH; ++i) {
-      for (int j = 0; j < DV; ++j) {
-        float s = 0.f;
-        for (int m = 0; m < CH; ++m) s += A[i * CH + m] * VB[m * DV + j];
-        U[i * DV + j] = s;
-      }
-      for (int j = 0; j < DK; ++j) {
-        float s = 0.f;
-        for (int m = 0; m < CH; ++m) s += A[i * CH + m] * KB[m * DK + j] * expf(G[m]);
-        W[i * DK + j] = s;
+      float* u = U + i * DV;
+      float* w = W + i * DK;
+      for (int j = 0; j < DV; ++j) u[j] = 0.f;
+      for (int j = 0; j < DK; ++j) w[j] = 0.f;
+      for (int m = 0; m < CH; ++m) {
+        const float a = A[i * CH + m];
+        for (int j = 0; j < DV; ++j) u[j] += a * VB[m * DV + j];
+        for (int j = 0; j < DK; ++j) w[j] += a * KB[m * DK + j];
       }
     }
     /* chunk step (:212-222) */
@@ -158,28 +175,43 @@ static void chunk_unit(const float* q, int64_t qs, const float* k, int64_t ks, c
         for (int kk = 0; kk < DK; ++kk) d += Q[i * DK + kk] * K[j * DK + kk];
         QK[i * CH + j] = d * DM[i * CH + j];
       }
-    for (int i = 0; i < CH; ++i)
-      for (int j = 0; j < DV; ++j) {
-        float s = 0.f;
-        for (int kk = 0; kk < DK; ++kk) s += W[i * DK + kk] * S[kk * DV + j];
-        VN[i * DV + j] = U[i * DV + j] - s;
+    for (int i = 0; i < CH; ++i) { /* v_new = value - k_cumdecay @ S */
+      for (int j = 0; j < DV; ++j) acc[j] = 0.f;
+      for (int kk = 0; kk < DK; ++kk) {
+        const float w = W[i * DK + kk];
+        for (int j = 0; j < DV; ++j) acc[j] += w * S[kk * DV + j];
       }
-    for (int i = 0; i < nv; ++i) {
-      const float eg = expf(G[i]);
-      for (int j = 0; j < DV; ++j) {
-        float inter = 0.f, intra = 0.f;
-        for (int kk = 0; kk < DK; ++kk) inter += Q[i * DK + kk] * eg * S[kk * DV + j];
-        for (int m = 0; m < CH; ++m) intra += QK[i * CH + m] * VN[m * DV + j];
-        out[((base + i) * HV + h) * DV + j] = inter + intra;
-      }
+      for (int j = 0; j < DV; ++j) VN[i * DV + j] = U[i * DV + j] - acc[j];
     }
-    const float gl = G[CH - 1], egl = expf(gl);
-    for (int kk = 0; kk < DK; ++kk)
-      for (int j = 0; j < DV; ++j) {
-        float s = 0.f;
-        for (int m = 0; m < CH; ++m) s += K[m * DK + kk] * expf(gl - G[m]) * VN[m * DV + j];
-        SN[kk * DV + j] = S[kk * DV + j] * egl + s;
+    for (int i = 0; i < nv; ++i) { /* out = (q * exp(g)) @ S + attn @ v_new */
+      float* o = out + ((base + i) * HV + h) * DV;
+      for (int j = 0; j < DV; ++j) acc[j] = 0.f;
+      for (int kk = 0; kk < DK; ++kk) {
+        const float qe = Q[i * DK + kk] * EG[i];
+        for (int j = 0; j < DV; ++j) acc[j] += qe * S[kk * DV + j];
       }
+      for (int j = 0; j < DV; ++j) o[j] = 0.f;
+      for (int m = 0; m < CH; ++m) {
+        const float a = QK[i * CH + m];
+        for (int j = 0; j < DV; ++j) o[j] += a * VN[m * DV + j];
+      }
+      for (int j = 0; j < DV; ++j) o[j] += acc[j];
+    }
+    /* S = S * exp(g_last) + (k * exp(g_last - g))^T @ v_new */
+    const float gl = G[CH - 1], egl = expf(gl);
+    for (int m = 0; m < CH; ++m) {
+      const float e = expf(gl - G[m]);
+      for (int kk = 0; kk < DK; ++kk) KE[m * DK + kk] = K[m * DK + kk] * e;
+    }
+    for (int kk = 0; kk < DK; ++kk) {
+      float* sn = SN + kk * DV;
+      for (int j = 0; j < DV; ++j) sn[j] = 0.f;
+      for (int m = 0; m < CH; ++m) {
+        const float a = KE[m * DK + kk];
+        for (int j = 0; j < DV; ++j) sn[j] += a * VN[m * DV + j];
+      }
+      for (int j = 0; j < DV; ++j) sn[j] += S[kk * DV + j] * egl;
+    }
     memcpy(S, SN, sizeof(float) * DK * DV);
   }
 }
@@ -191,8 +223,8 @@ void gdn_ref_chunk_prefill(const float* q, int64_t qs, const float* k, int64_t k
                            const int32_t* cu, int n_seqs, int HK, int HV, int DK, int DV,
                            float scale, float* out) {
   const int rep = HV / HK;
-  const size_t work_floats = (size_t)CH * (4 * DK + 3 * DV) + 3 * CH * CH + (size_t)DK * DV +
-                             (size_t)CH * DV;
+  const size_t work_floats = (size_t)CH * (5 * DK + 4 * DV) + 3 * CH * CH + (size_t)DK * DV +
+                             (size_t)(DK > DV ? DK : DV);
 #pragma omp parallel
   {
     float* work = (float*)malloc(sizeof(float) * work_floats);
