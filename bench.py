@@ -56,6 +56,7 @@ def parse():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-prefill", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-config4", action="store_true")
     ap.add_argument("--prefill-steps", type=int, default=3)
     ap.add_argument("--profile-case", default=None,
                     choices=["recurrent", "decode_fused", "conv_decode", "conv_varlen", "chunk",
@@ -218,39 +219,194 @@ class DecodeStack:
             self.graph.replay()
 
 
+C3 = dict(layers=24, attn_every=4, hidden=2048, HK=16, DK=128, HV=32, DV=128, K=4, q_heads=16,
+          kv_heads=4, head_dim=128, inter=6144, vocab=151936, bs=128, ctx_lo=256, ctx_hi=4096,
+          gen=256, slots=256, eps=1e-6)
+
+
+def _add_rms(h, r, w, eps):
+    """Fused residual add + RMSNorm of the decoder chain (models/qwen3.py's
+    RMSNorm with a residual): r <- h + r, h <- rmsnorm(r) * w."""
+    r = h if r is None else (h.float() + r.float()).to(h.dtype)
+    x = r.float()
+    x = x * torch.rsqrt(x.pow(2).mean(-1, keepdim=True) + eps)
+    return (x * w.float()).to(h.dtype), r
+
+
+class HybridStage:
+    """One pipeline stage of a config-3-shaped hybrid decoder (decode step):
+    the stage's contiguous range of the 24 layers (split_layers, 3 per stage
+    at 8 stages), every 4th layer full attention and the rest GatedDeltaNet
+    (this package's layer), each followed by a SwiGLU MLP (6144), with the
+    fused residual chain (hidden, residual) between layers; the first stage
+    embeds the tokens (vocab 151,936), the last applies the final norm and the
+    LM head and takes the greedy token.  Attention is GQA 16 q / 4 kv heads x
+    128 through torch SDPA over a contiguous KV cache whose length is the mean
+    config-3 context (prompts U[256, 4096] plus half of 256 generated tokens:
+    2304): the attention layers' weights and KV bytes are config 3's, but the
+    KV cache is not paged.  Weights random (seeded); the whole stage step is
+    one CUDA graph."""
+
+    def __init__(self, pkg, dev, seed, lo, hi, first, last):
+        c = C3
+        self.pkg, self.dev, self.first, self.last = pkg, dev, first, last
+        H, bs = c["hidden"], c["bs"]
+        g = torch.Generator(device=dev).manual_seed(seed)
+
+        def nrm(*shape, std):
+            return (torch.randn(*shape, generator=g, device=dev) * std).to(torch.bfloat16)
+
+        cfg = type("Cfg", (), dict(hidden_size=H, linear_num_key_heads=c["HK"],
+                                   linear_num_value_heads=c["HV"], linear_key_head_dim=c["DK"],
+                                   linear_value_head_dim=c["DV"], linear_conv_kernel_dim=c["K"],
+                                   rms_norm_eps=c["eps"]))
+        self.ctx_len = (c["ctx_lo"] + c["ctx_hi"]) // 2 + c["gen"] // 2
+        self.layers = []
+        gdn = []
+        prev = torch.get_default_dtype()
+        torch.set_default_dtype(torch.bfloat16)
+        try:
+            for i in range(lo, hi):
+                L = {"ln1": torch.ones(H, dtype=torch.bfloat16, device=dev),
+                     "ln2": torch.ones(H, dtype=torch.bfloat16, device=dev),
+                     "gate_up": nrm(2 * c["inter"], H, std=H ** -0.5),
+                     "down": nrm(H, c["inter"], std=c["inter"] ** -0.5)}
+                if (i + 1) % c["attn_every"] == 0:
+                    qd, kd = c["q_heads"] * c["head_dim"], c["kv_heads"] * c["head_dim"]
+                    L["qkv"] = nrm(qd + 2 * kd, H, std=H ** -0.5)
+                    L["o"] = nrm(H, qd, std=qd ** -0.5)
+                    L["k_cache"] = nrm(bs, c["kv_heads"], self.ctx_len, c["head_dim"], std=1.0)
+                    L["v_cache"] = nrm(bs, c["kv_heads"], self.ctx_len, c["head_dim"], std=1.0)
+                else:
+                    with torch.device(dev), torch.no_grad():
+                        m = pkg.layer.Qwen3_5GatedDeltaNet(cfg)
+                        m._fused_weight().normal_(0, H ** -0.5, generator=g)
+                        m.conv1d.weight.uniform_(-0.5, 0.5, generator=g)
+                        m.A_log.uniform_(-1.0, 0.0, generator=g)
+                        m.dt_bias.zero_()
+                        m.out_proj.weight.normal_(0, (c["HV"] * c["DV"]) ** -0.5, generator=g)
+                    L["gdn"] = m
+                    gdn.append(m)
+                self.layers.append(L)
+        finally:
+            torch.set_default_dtype(prev)
+        if gdn:
+            self.pools = pkg.state_pool.StatePools(gdn, c["slots"], dev)
+            with torch.no_grad():
+                self.pools.s_pool.normal_(0, 0.02, generator=g)
+        perm = torch.randperm(c["slots"], generator=torch.Generator().manual_seed(seed))
+        self.ids = perm[:bs].to(dev)
+        self.cu = torch.arange(bs + 1, dtype=torch.int32, device=dev)
+        self.embed = nrm(c["vocab"], H, std=1.0) if first else None
+        self.lm_head = nrm(c["vocab"], H, std=H ** -0.5) if last else None
+        self.final_ln = torch.ones(H, dtype=torch.bfloat16, device=dev)
+        self.tokens = torch.randint(0, c["vocab"], (bs,), generator=g, device=dev)
+        self.x_h = torch.randn(bs, H, generator=g, device=dev).to(torch.bfloat16)
+        self.x_r = torch.randn(bs, H, generator=g, device=dev).to(torch.bfloat16)
+        self.graph = None
+
+    def _attn(self, L, h):
+        c = C3
+        bs, qh, kh, hd = h.shape[0], c["q_heads"], c["kv_heads"], c["head_dim"]
+        qkv = torch.nn.functional.linear(h, L["qkv"])
+        q = qkv[:, :qh * hd].view(bs, qh, 1, hd)
+        o = torch.nn.functional.scaled_dot_product_attention(q, L["k_cache"], L["v_cache"],
+                                                             enable_gqa=True)
+        return torch.nn.functional.linear(o.reshape(bs, qh * hd), L["o"])
+
+    def _step(self):
+        eps = C3["eps"]
+        if self.first:
+            h, r = self.embed[self.tokens], None
+        else:
+            h, r = self.x_h, self.x_r
+        for L in self.layers:
+            h, r = _add_rms(h, r, L["ln1"], eps)
+            h = self._attn(L, h) if "qkv" in L else L["gdn"](None, h)
+            h, r = _add_rms(h, r, L["ln2"], eps)
+            gu = torch.nn.functional.linear(h, L["gate_up"])
+            a, b = gu.chunk(2, dim=-1)
+            h = torch.nn.functional.linear(torch.nn.functional.silu(a) * b, L["down"])
+        if self.last:
+            h, _ = _add_rms(h, r, self.final_ln, eps)
+            return torch.nn.functional.linear(h, self.lm_head).argmax(-1), None
+        return h, r
+
+    def capture(self):
+        ctx = self.pkg.context
+        ctx.set_context(self.cu, self.cu, 1, 1, linear_state_ids=self.ids)
+        with torch.inference_mode():
+            for _ in range(2):
+                self.y_h, self.y_r = self._step()
+            torch.cuda.synchronize()
+            self.graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(self.graph):
+                self.y_h, self.y_r = self._step()
+        ctx.reset_context()
+
+    def replay(self):
+        self.graph.replay()
+
+
 def pp_bench(pkg, dev, world, rank, steps, warmup):
-    """The config-1 decode stack as a `world`-stage pipeline: stage r runs its
-    contiguous layer range (split_layers) and hands (hidden, residual) to stage
-    r+1 through PipelineHandoff (one packed NCCL message on a side stream,
-    double-buffered, ordered by events) — the reference's two blocking
-    send/recv per boundary (engine/model_runner.py:795-810) replaced.  Stage r
-    starts step i+1 as soon as it has sent step i, so stages overlap across
-    steps.  Exposed handoff = (pipelined time - (K + S - 1) slowest-stage
-    compute steps) / pipelined time for K steps through S stages (the pipeline
-    fills once), CUDA-event timed, max over ranks."""
-    c = C1
+    """Config-3-shaped hybrid decoder (HybridStage) as a `world`-stage
+    pipeline, decode steps of 128 sequences.  Stage r hands (hidden,
+    residual) to stage r + 1 through PipelineHandoff — one packed NCCL
+    message per boundary on a side stream and on that boundary's own
+    two-rank process group, double-buffered and event-ordered — in place of
+    the reference's two blocking send / recv calls per boundary
+    (engine/model_runner.py:795-810).  Stage r starts step i + 1 as soon as
+    it has queued step i, so successive steps (independent micro-batches)
+    overlap across stages.
+
+    Three timings, CUDA events, max over ranks, `steps` steps each:
+      t_stage  each stage's graph alone (no handoff)
+      t_local  each stage with the handoff replaced by local copies of the
+               same bytes (the receive buffer copied in, the output copied out)
+      t_pp     the pipeline with the NCCL handoff
+    K steps through S stages take K + S - 1 stage steps even with a free
+    handoff (the pipeline fills once), so exposed handoff = (t_pp - fill -
+    t_local) / t_pp with fill = (S - 1) t_local / K."""
+    c = C3
     P = pkg.parallel
     lo, hi = P.split_layers(c["layers"], world, rank)
-    n_layers = max(0, hi - lo)   # the ceil split leaves the last stages empty at 8 stages
     prev, nxt = P.pp_peers(rank, 1, world)
-    stack = DecodeStack(pkg, dev, seed=4321 + rank, layers=n_layers)
-    stack.capture()
-    ho = P.PipelineHandoff(c["hidden"], c["bs"], torch.bfloat16, dev, prev, nxt, mode="packed")
+    groups = P.boundary_groups(world)
+    stage = HybridStage(pkg, dev, seed=4321 + rank, lo=lo, hi=hi, first=prev is None,
+                        last=nxt is None)
+    stage.capture()
+    ho = P.PipelineHandoff(c["hidden"], c["bs"], torch.bfloat16, dev, prev, nxt, mode="packed",
+                           recv_group=groups[rank - 1] if prev is not None else None,
+                           send_group=groups[rank] if nxt is not None else None)
+    rbuf = torch.empty(2, c["bs"], c["hidden"], dtype=torch.bfloat16, device=dev)
+    sbuf = torch.empty_like(rbuf)
 
     def stage_only():
-        stack.replay()
+        stage.replay()
+
+    def local_step():
+        if prev is not None:
+            stage.x_h.copy_(rbuf[0])
+            stage.x_r.copy_(rbuf[1])
+        stage.replay()
+        if nxt is not None:
+            sbuf[0].copy_(stage.y_h)
+            sbuf[1].copy_(stage.y_r)
 
     def pp_step():
         if prev is not None:
-            h, _ = ho.recv(c["bs"])
-            stack.x.copy_(h)
-        stack.replay()
+            h, r = ho.recv(c["bs"])
+            stage.x_h.copy_(h)
+            stage.x_r.copy_(r)
+        stage.replay()
         if nxt is not None:
-            ho.send(stack.y, stack.x)
+            ho.send(stage.y_h, stage.y_r)
 
-    for _ in range(warmup):
-        stage_only()
-    t_stage = time_region(stage_only, steps, world)      # max over ranks
+    for fn in (stage_only, local_step):
+        for _ in range(warmup):
+            fn()
+    t_stage = time_region(stage_only, steps, world)
+    t_local = time_region(local_step, steps, world)
     for _ in range(warmup):
         pp_step()
     ho.flush()
@@ -259,21 +415,25 @@ def pp_bench(pkg, dev, world, rank, steps, warmup):
     ho.flush()
     torch.cuda.synchronize()
     barrier(world)
-    # K pipelined steps through S stages take (K + S - 1) stage-steps even with a
-    # free handoff (the pipeline fills once); what is left over is the handoff
-    fill = (world - 1) * t_stage / steps
-    exposed = max(0.0, (t_pp - t_stage - fill) / t_pp)
-    per_stage = [max(0, b - a) for a, b in (P.split_layers(c["layers"], world, r)
-                                             for r in range(world))]
-    out = {"stages": world, "layers_per_stage": per_stage,
-           "handoff": "PipelineHandoff packed (hidden, residual) over NCCL, side stream",
-           "bytes_per_handoff": 2 * c["bs"] * c["hidden"] * 2,
+    fill = (world - 1) * t_local / steps
+    exposed = (t_pp - fill - t_local) / t_pp
+    per_stage = [b - a for a, b in (P.split_layers(c["layers"], world, r) for r in range(world))]
+    out = {"workload": "config3-shaped hybrid decoder, decode steps of 128 sequences: 24 layers "
+                       "(every 4th full attention GQA 16q/4kv x 128 over a 2304-token KV cache, "
+                       "the rest GDN), SwiGLU 6144, vocab 151936, bf16; embedding on the first "
+                       "stage, final norm + LM head + greedy token on the last",
+           "stages": world, "layers_per_stage": per_stage,
+           "handoff": "PipelineHandoff packed (hidden, residual), NCCL send/recv on a side "
+                      "stream, one two-rank process group per boundary",
+           "bytes_per_handoff": 2 * c["bs"] * c["hidden"] * 2, "steps": steps,
            "ms_per_step_pipelined": round(t_pp / steps * 1e3, 4),
+           "ms_per_step_local_copy": round(t_local / steps * 1e3, 4),
            "ms_per_step_slowest_stage": round(t_stage / steps * 1e3, 4),
            "pipeline_fill_ms": round(fill * 1e3, 4),
+           "exposed_handoff_ms_per_step": round((t_pp - fill - t_local) / steps * 1e3, 4),
            "exposed_handoff_frac": round(exposed, 4),
            "tok_s_pipelined": round(c["bs"] * steps / t_pp, 1)}
-    stack.graph = None
+    stage.graph = None
     return out
 
 
@@ -519,6 +679,294 @@ def prefill_bench(pkg, device, steps, peaks):
                              "peak": peaks["bf16_tflops"], "peak_source": peaks["source"],
                              "frac": round(achieved / peaks["bf16_tflops"], 5),
                              "algorithmic_flops": flops, "clocks": chunk_clk}}
+
+
+# ---------------------------------------------------------------------------
+# config-2 prefill with the v-heads sharded over the ranks (tensor parallel)
+# ---------------------------------------------------------------------------
+
+
+def config2_lens():
+    c = C2
+    rng = np.random.Generator(np.random.PCG64(2))
+    return rng.integers(c["len_lo"], c["len_hi"] + 1, size=c["n_seqs"]).tolist()
+
+
+def config2_cfg():
+    c = C2
+    return type("Cfg", (), dict(hidden_size=c["hidden"], linear_num_key_heads=c["HK"],
+                                linear_num_value_heads=c["HV"], linear_key_head_dim=c["DK"],
+                                linear_value_head_dim=c["DV"], linear_conv_kernel_dim=c["K"],
+                                rms_norm_eps=1e-6))
+
+
+def config2_full_weights(device, seed):
+    """Full (unsharded) config-2 layer weights from a seeded device generator:
+    every rank draws the same tensors."""
+    c = C2
+    H, HK, HV, D, K = c["hidden"], c["HK"], c["HV"], c["DK"], c["K"]
+    cd = 2 * HK * D + HV * D
+    g = torch.Generator(device=device).manual_seed(seed)
+
+    def nrm(*shape, std):
+        return (torch.randn(*shape, generator=g, device=device) * std).to(torch.bfloat16)
+
+    return {"in_proj_qkv.weight": nrm(cd, H, std=H ** -0.5),
+            "in_proj_z.weight": nrm(HV * D, H, std=H ** -0.5),
+            "in_proj_b.weight": nrm(HV, H, std=H ** -0.5),
+            "in_proj_a.weight": nrm(HV, H, std=H ** -0.5),
+            "conv1d.weight": ((torch.rand(cd, 1, K, generator=g, device=device) - 0.5)
+                              .to(torch.bfloat16)),
+            "A_log": (-torch.rand(HV, generator=g, device=device)).to(torch.bfloat16),
+            "dt_bias": torch.zeros(HV, dtype=torch.bfloat16, device=device),
+            "norm.weight": torch.ones(D, dtype=torch.bfloat16, device=device),
+            "out_proj.weight": nrm(H, HV * D, std=(HV * D) ** -0.5)}
+
+
+def build_loaded_layer(pkg, cfg, weights, device, parallel=None):
+    """A layer on `device` whose parameters are loaded from full weights through
+    the layer's own weight loaders (the engine's load path), so a sharded
+    layer takes its rank's heads."""
+    prev = torch.get_default_dtype()
+    torch.set_default_dtype(torch.bfloat16)
+    try:
+        with torch.device(device):
+            m = pkg.layer.Qwen3_5GatedDeltaNet(cfg, parallel=parallel)
+    finally:
+        torch.set_default_dtype(prev)
+    with torch.no_grad():
+        for name, w in weights.items():
+            p = m.get_parameter(name)
+            getattr(p, "weight_loader", lambda p_, w_: p_.data.copy_(w_))(p, w)
+    return m
+
+
+def tp_prefill_bench(pkg, dev, world, rank, steps):
+    """Config-2 varlen prefill of one layer with the 32 v-heads (and the
+    matching k-heads) sharded over the `world` ranks as the reference's
+    tensor parallelism shards them (qwen3_5.py:796-835): each rank runs the
+    projection GEMM of its heads, the conv / chunk kernels on its heads and
+    the out_proj partial product, which an NCCL all-reduce sums
+    (layers/linear.py:154-158).  Strong scaling: the same 282,505 tokens at
+    every N.  Reports tok/s (max-over-ranks step time), the efficiency
+    against the unsharded layer on one of these GPUs, the all-reduce's share,
+    and tp_parity: every rank also runs the unsharded layer from the same
+    seeds and compares the all-reduced output and its own heads' final
+    states."""
+    c = C2
+    P = pkg.parallel
+    P.init_parallel_state(rank, world, tp_size=world, pp_size=1)
+    lens = config2_lens()
+    N = int(sum(lens))
+    cfg = config2_cfg()
+    W = config2_full_weights(dev, seed=11)
+    m = build_loaded_layer(pkg, cfg, W, dev)                      # this rank's shard
+    one = type("OneRank", (), dict(get_tp_rank=staticmethod(lambda: 0),
+                                   get_tp_size=staticmethod(lambda: 1),
+                                   get_tp_group=staticmethod(lambda: None)))
+    ref = build_loaded_layer(pkg, cfg, W, dev, parallel=one)      # the whole layer
+    del W
+    pools = pkg.state_pool.StatePools([m], c["n_seqs"], dev)
+    ref_pools = pkg.state_pool.StatePools([ref], c["n_seqs"], dev)
+    ids = torch.randperm(c["n_seqs"], generator=torch.Generator().manual_seed(4)).to(dev)
+    cu = torch.tensor(np.concatenate([[0], np.cumsum(lens)]), dtype=torch.int32, device=dev)
+    g = torch.Generator(device=dev).manual_seed(3)
+    x = torch.randn(N, c["hidden"], generator=g, device=dev).to(torch.bfloat16)
+    ctx = pkg.context
+
+    def run(layer, pl):
+        pl.reset(ids)                          # fresh prefill: zero slots
+        ctx.set_context(cu, cu, max(lens), max(lens), linear_state_ids=ids, lens_q=lens)
+        try:
+            with torch.inference_mode():
+                return layer(None, x)
+        finally:
+            ctx.reset_context()
+
+    for _ in range(2):
+        run(m, pools)
+        run(ref, ref_pools)
+    torch.cuda.synchronize()
+    t_tp = time_region(lambda: run(m, pools), steps, world)
+    t_one = time_region(lambda: run(ref, ref_pools), steps, world)
+    # the out_proj all-reduce alone, on the same [N, hidden] bf16 shape
+    y = torch.empty(N, c["hidden"], dtype=torch.bfloat16, device=dev)
+    grp = P.get_tp_group()
+    for _ in range(2):
+        torch.distributed.all_reduce(y, group=grp)
+    t_ar = time_region(lambda: torch.distributed.all_reduce(y, group=grp), steps, world)
+    del y
+    # parity: one fresh prefill through both layers
+    y_tp = run(m, pools)
+    y_ref = run(ref, ref_pools)
+    torch.cuda.synchronize()
+    out_err = (y_tp.float() - y_ref.float()).abs().max().item()
+    out_mag = y_ref.float().abs().max().item()
+    hv = slice(rank * m.num_v_heads, (rank + 1) * m.num_v_heads)
+    a, b = m.s_cache[ids], ref.s_cache[ids][:, hv]
+    state_rel = max(((a[i] - b[i]).norm() / b[i].norm().clamp_min(1e-30)).item()
+                    for i in range(a.shape[0]))
+    errs = torch.tensor([out_err, state_rel], dtype=torch.float64, device=dev)
+    if world > 1:
+        torch.distributed.all_reduce(errs, op=torch.distributed.ReduceOp.MAX)
+    out_err, state_rel = errs.tolist()
+    pkg.ops.check_status(dev)
+    per_step = t_tp / steps
+    flops = CHUNK_FLOPS_PER_TOKEN_HEAD * N * c["HV"]
+    res = {"workload": f"config2 prefill, 1 GDN layer, {N} tokens (64 seqs, lens U[128,8192] "
+                       f"seed 2), v-heads sharded {world} ways",
+           "parallelism": f"tp{world}", "scaling": "strong",
+           "v_heads_per_gpu": m.num_v_heads, "k_heads_per_gpu": m.num_k_heads,
+           "value": round(N / per_step, 1), "unit": "tok/s",
+           "ms_per_step": round(per_step * 1e3, 3), "steps": steps,
+           "ms_per_step_unsharded_1gpu": round(t_one / steps * 1e3, 3),
+           "efficiency_vs_1gpu": round((t_one / steps) / (world * per_step), 4),
+           "allreduce": {"what": f"NCCL all_reduce of the out_proj output [{N}, "
+                                 f"{c['hidden']}] bf16", "ms": round(t_ar / steps * 1e3, 3),
+                         "share_of_step": round((t_ar / steps) / per_step, 4)},
+           "chunk_tflops_per_gpu": round(flops / world / per_step / 1e12, 1),
+           "tp_parity": {"vs": "the unsharded layer from the same seeds on each rank",
+                         "out_max_abs": out_err, "out_ref_max_abs": round(out_mag, 3),
+                         "state_rel_max": state_rel,
+                         "tolerance": {"out_max_abs": 2e-2, "state_rel": 2e-2},
+                         "pass": bool(out_err <= 2e-2 and state_rel <= 2e-2)}}
+    del m, ref, pools, ref_pools, x, y_tp, y_ref
+    torch.cuda.empty_cache()
+    return res
+
+
+# ---------------------------------------------------------------------------
+# config 4: long-context prefill + decode, v-heads over 8 GPUs
+# ---------------------------------------------------------------------------
+
+C4 = dict(n_seqs=8, seq_len=131072, shards=8, decode_steps=1024)
+
+
+def config4_bench(pkg, dev, world, rank, peaks):
+    """Config 4: 8 sequences of 131,072 tokens through one GDN layer at
+    config-2 head shapes, chunked prefill then 1024 decode steps, the 32
+    v-heads sharded 8 ways (4 v-heads / 2 k-heads per GPU).  At 8 ranks each
+    rank runs its shard and out_proj all-reduces over NCCL; on 1 GPU the
+    bench runs shard 0 of 8 (the same per-GPU kernels and bytes; the
+    all-reduce across shards is not run).  Reports the prefill layer time,
+    the chunk prefill kernels alone against the bf16 tensor roofline, the
+    decode step (one layer forward per step, captured in a CUDA graph) and
+    the fused decode core alone against HBM (state bytes 2 x 8 x 4 x 64 KiB
+    per step per GPU)."""
+    c, c4 = C2, C4
+    shards = c4["shards"]
+    assert world in (1, shards)
+    tp_rank = rank if world == shards else 0
+    P = pkg.parallel
+    if world == shards:
+        P.init_parallel_state(rank, world, tp_size=world, pp_size=1)
+        par = None
+    else:
+        par = type("OneShardOf8", (), dict(get_tp_rank=staticmethod(lambda: 0),
+                                          get_tp_size=staticmethod(lambda: shards),
+                                          get_tp_group=staticmethod(lambda: None)))
+    W = config2_full_weights(dev, seed=13)
+    m = build_loaded_layer(pkg, config2_cfg(), W, dev, parallel=par)
+    del W
+    if world == 1:
+        m.out_proj.tp_size = 1           # the partial sum of this shard; no peers to reduce with
+    n, T = c4["n_seqs"], c4["seq_len"]
+    lens = [T] * n
+    N = n * T
+    pools = pkg.state_pool.StatePools([m], n, dev)
+    ids = torch.randperm(n, generator=torch.Generator().manual_seed(9)).to(dev)
+    cu = torch.tensor(np.concatenate([[0], np.cumsum(lens)]), dtype=torch.int32, device=dev)
+    g = torch.Generator(device=dev).manual_seed(21)
+    x = torch.randn(N, c["hidden"], generator=g, device=dev).to(torch.bfloat16)
+    ctx = pkg.context
+
+    def prefill():
+        pools.reset(ids)
+        ctx.set_context(cu, cu, T, T, linear_state_ids=ids, lens_q=lens)
+        try:
+            with torch.inference_mode():
+                return m(None, x)
+        finally:
+            ctx.reset_context()
+
+    prefill()
+    torch.cuda.synchronize()
+    t_pre = time_region(prefill, 2, world) / 2
+    # the chunk prefill kernels alone on this shard's heads (conv output of the layer's q/k/v)
+    with torch.inference_mode():
+        proj = torch.nn.functional.linear(x, m._fused_weight())
+        y = pkg.ops.causal_conv_silu_varlen(proj[:, :m.conv_dim], m.conv_cache, ids,
+                                            m.conv1d.weight, cu)
+        r = m._proj_rows
+        gg, beta = pkg.ops.fused_g_beta(proj[:, r[1]:r[2]], proj[:, r[2]:r[3]],
+                                        m.A_log[m._v_head_slice], m.dt_bias[m._v_head_slice])
+        del proj
+        q, k, v = m._split(y)
+        chunk = lambda: pkg.ops.chunk_gated_delta_rule_varlen(q, k, v, gg, beta, m.s_cache, ids,
+                                                              cu, T)
+        chunk()
+        torch.cuda.synchronize()
+        t_chunk = time_region(chunk, 3, world) / 3
+        del q, k, v, y, gg, beta
+    torch.cuda.empty_cache()
+    flops = CHUNK_FLOPS_PER_TOKEN_HEAD * N * m.num_v_heads
+    # decode: states from a fresh prefill, then 1024 steps of one token per sequence
+    prefill()
+    cu1 = torch.arange(n + 1, dtype=torch.int32, device=dev)
+    h = torch.randn(n, c["hidden"], generator=g, device=dev).to(torch.bfloat16)
+    ctx.set_context(cu1, cu1, 1, 1, linear_state_ids=ids)
+    try:
+        with torch.inference_mode():
+            for _ in range(2):
+                yd = m(None, h)
+            torch.cuda.synchronize()
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph):
+                yd = m(None, h)
+    finally:
+        ctx.reset_context()
+    steps = c4["decode_steps"]
+    t_dec = time_region(graph.replay, steps, world) / steps
+    del graph
+    # the fused decode core alone (the kernel the decode step runs), CUDA events
+    bs, HK, HV, D = n, m.num_k_heads, m.num_v_heads, c["DK"]
+    pj = torch.randn(bs, m._fused_weight().shape[0], generator=g, device=dev).to(torch.bfloat16)
+    rr = m._proj_rows
+    core = lambda: pkg.ops.decode_fused(
+        pj[:, :m.conv_dim], pj[:, rr[0]:rr[1]].view(bs, HV, D), pj[:, rr[1]:rr[2]],
+        pj[:, rr[2]:rr[3]], m.conv_cache, m.conv1d.weight.view(m.conv_dim, m.conv_kernel),
+        m.A_log[m._v_head_slice], m.dt_bias[m._v_head_slice], m.s_cache, ids, m.norm.weight,
+        m.norm.eps)
+    with torch.inference_mode():
+        for _ in range(3):
+            core()
+        torch.cuda.synchronize()
+        t_core = time_region(core, 200, world) / 200
+    dec_bytes = decode_algorithmic_bytes(bs, HK, HV, D, c["K"])
+    state_bytes = 2 * bs * HV * D * D * 4
+    pkg.ops.check_status(dev)
+    res = {"workload": f"config4: {n} sequences x {T} tokens, 1 GDN layer at config-2 head "
+                       f"shapes, v-heads sharded {shards} ways ({HV} v / {HK} k heads per GPU)"
+                       + ("" if world == shards else "; this run: shard 0 of 8 on one GPU, "
+                          "without the cross-shard all-reduce"),
+           "prefill": {"ms": round(t_pre * 1e3, 3), "tok_s": round(N / t_pre, 1),
+                       "chunk_kernels_ms": round(t_chunk * 1e3, 3),
+                       "chunk_chain_column_parts": 2 if n * HV < 2 * 148 else 1,
+                       "chunk_tflops": round(flops / t_chunk / 1e12, 2),
+                       "chunk_frac_of_bf16_peak": round(flops / t_chunk / 1e12 /
+                                                        peaks["bf16_tflops"], 4)},
+           "decode": {"steps": steps, "ms_per_step": round(t_dec * 1e3, 4),
+                      "tok_s": round(n / t_dec, 1),
+                      "core_kernel_us": round(t_core * 1e6, 2),
+                      "core_state_gbs": round(state_bytes / t_core / 1e9, 1),
+                      "core_achieved_gbs": round(dec_bytes / t_core / 1e9, 1),
+                      "core_frac_of_hbm": round(dec_bytes / t_core / 1e9 / peaks["hbm_gbs"], 4),
+                      "algorithmic_bytes_per_launch": dec_bytes,
+                      "note": "32 (sequence, v-head) units per GPU: one 64 KiB state each; "
+                              "the launch is latency-bound, far from the HBM roofline"}}
+    del m, pools, x, pj
+    torch.cuda.empty_cache()
+    return res
 
 
 # ---------------------------------------------------------------------------
@@ -818,7 +1266,13 @@ def main():
             "clocks": clk}
 
     if world > 1:
-        line["pp"] = pp_bench(pkg, dev, world, rank, min(args.steps, 200), args.warmup)
+        del stack.graph
+        stack = None
+        torch.cuda.empty_cache()
+        line["tp_prefill"] = tp_prefill_bench(pkg, dev, world, rank, steps=5)
+        line["pp"] = pp_bench(pkg, dev, world, rank, max(args.steps, 400), args.warmup)
+        if world == C4["shards"] and not args.no_config4:
+            line["config4"] = config4_bench(pkg, dev, world, rank, peaks)
     if rank == 0 and world == 1 and not args.no_prefill:
         try:
             line["prefill"] = prefill_bench(pkg, dev, args.prefill_steps, peaks)
@@ -826,11 +1280,17 @@ def main():
                 line["prefill"]["chunk_kernel"]["cpu_baseline"] = cpu_prefill_baseline()
         except Exception as e:  # reported, never hides the headline
             line["prefill"] = {"error": repr(e)[:300]}
+    if world == 1 and not args.no_config4:
+        try:
+            line["config4"] = config4_bench(pkg, dev, world, rank, peaks)
+        except Exception as e:  # reported, never hides the headline
+            line["config4"] = {"error": repr(e)[:300]}
     if rank == 0 and world == 1 and not args.no_cpu:
         line["cpu_baseline"] = cpu_baseline()
     if rank == 0:
         print(json.dumps(line), flush=True)
-    del stack.graph
+    if stack is not None:
+        del stack.graph
     if world > 1:
         torch.distributed.barrier()
         torch.distributed.destroy_process_group()

@@ -61,6 +61,18 @@ int gdn_abi_version(void);
 const char* gdn_last_error(void);
 
 /*
+ * Diagnostic for testing the bounded device-side waits (no counterpart in the
+ * reference).  Sets, process-wide, the number of polls after which the wait of
+ * gdn_decode_fused's head-per-CTA form for its state bulk copy gives up: that
+ * launch then ORs GDN_STATUS_TIMEOUT into *status, waits (with the normal
+ * limit) for the copy it has in flight, leaves the recurrent state untouched
+ * and returns; the context stays usable.  0 makes the wait give up at once;
+ * a negative value restores the default.  Not for production use: calls made
+ * while an override is set give invalid results by design.
+ */
+void gdn_set_wait_limit(int64_t polls);
+
+/*
  * (b) Fused gate.  Replaces fused_g_beta / _gdn_g_beta_kernel
  * (qwen3_5.py:320-360).
  *   g[r,h]    = -exp(a_log[h]) * softplus(a[r,h] + dt_bias[h])   (fp32;

@@ -29,6 +29,7 @@ vp, i32, i64, f32 = C.c_void_p, C.c_int32, C.c_int64, C.c_float
 SIGNATURES = {
     "gdn_abi_version": [],
     "gdn_last_error": [],
+    "gdn_set_wait_limit": [i64],
     "gdn_fused_g_beta": [vp, vp, i64, i64, i32, vp, vp, i32, vp, vp, vp, vp],
     "gdn_conv_decode_step": [vp, i64, vp, i64, i64, vp, i32, i32, i32, vp, vp, i64, vp, vp],
     "gdn_causal_conv_silu_varlen": [vp, i64, vp, i64, i64, vp, vp, i32, i64, i32, i32, vp, vp,
@@ -62,7 +63,7 @@ def load() -> C.CDLL:
     for name, argtypes in SIGNATURES.items():
         fn = getattr(lib, name)
         fn.argtypes = argtypes
-        fn.restype = {"gdn_last_error": C.c_char_p,
+        fn.restype = {"gdn_last_error": C.c_char_p, "gdn_set_wait_limit": None,
                       "gdn_chunk_prefill_workspace_bytes": C.c_int64}.get(name, C.c_int)
     _LIB = lib
     return lib

@@ -333,11 +333,30 @@ __global__ void __launch_bounds__(kPrepThreads, kPrepCtasPerSm) chunk_prep_kerne
 }
 
 // ---------------------------------------------------------------- chain
+// One CTA per (sequence, v-head, column part): NCOL of the state's 128 value
+// columns (128: the whole state; 64: half of it, for launches with too few
+// chains to fill the GPU — a long-context prefill of a few sequences).  The
+// delta rule's value columns evolve independently given the chunk's K, Q, T
+// and M2, so the parts of a chain need no exchange; each loads the shared K /
+// Q / [T; M2] tiles itself.  8 warps: warp w owns TMEM lane quarter w % 4 and
+// CPT = NCOL / 2 columns of the part (group w / 4).
+// CG groups of 32 TMEM columns (starting at `ta`) behind one wait.
+template <int CG>
+__device__ __forceinline__ void tmem_ld_groups(uint32_t ta, float (&v)[CG][32]) {
+  if constexpr (CG == 2) {
+    tmem_ld32x2(ta, ta + 32, v[0], v[1]);
+  } else {
+    tmem_ld32(ta, v[0]);
+  }
+}
+
+template <int NCOL>
 struct __align__(1024) ChainSmem {
+  static constexpr int NB = NCOL / 64;   // 64-column blocks of the part
   uint8_t kq[2][128 * 128];   // [dk block][row][128 B]: K / Q rows interleaved (ilv_row)
-  uint8_t scratch[32768];     // the bf16 S tile for MMA 3, then R, then W (hi / lo)
+  uint8_t scratch[NB * 16384];// the bf16 S tile for MMA 3, then R, then W (hi / lo)
   uint8_t a4[128 * 128];      // [T ; M2] from the chunk's block, then the out tile
-  uint8_t v[2][64 * 128];     // [dv block][token row][128 B]
+  uint8_t v[NB][64 * 128];    // [dv block][token row][128 B]
   float f[2][5][kC];          // the blocks' per-token factors, chunks c and c + 1
   unsigned long long mbar;    // MMA completion
   unsigned long long lbar[5]; // loads: K, Q, V, [T;M2] tile, factors
@@ -345,6 +364,7 @@ struct __align__(1024) ChainSmem {
   int abort;
 };
 
+template <int NCOL>
 __global__ void __launch_bounds__(kChainThreads, 2) chunk_chain_kernel(
     const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
     const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_out,
@@ -352,17 +372,25 @@ __global__ void __launch_bounds__(kChainThreads, 2) chunk_chain_kernel(
     const int32_t* __restrict__ chunk_start, float* __restrict__ pool, int64_t slot_stride,
     int64_t num_slots, const int64_t* __restrict__ ids, const int32_t* __restrict__ cu,
     int64_t n_tokens, int max_seqlen, bf16* __restrict__ out, int HK, int HV, int32_t* status) {
+  constexpr int PARTS = kD / NCOL;        // column parts per chain
+  constexpr int NB = NCOL / 64;           // 64-column blocks per part
+  constexpr int CPT = NCOL / 2;           // columns per thread
+  constexpr int CG = CPT / 32;            // 32-column TMEM loads per thread
+  static_assert(NCOL == 128 || NCOL == 64, "column parts of 128 or 64");
+  using Smem = ChainSmem<NCOL>;
   extern __shared__ uint8_t smem_raw[];
-  ChainSmem& sm = *reinterpret_cast<ChainSmem*>(
+  Smem& sm = *reinterpret_cast<Smem*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int qd = warp & 3, half = warp >> 2;
   const int row = qd * 32 + lane;        // TMEM lane: dk row of S, or row of a 128-row tile
   const bool second = qd & 1;            // interleaved tile row of the second half (Q / M2)
-  const int rank = blockIdx.x / HV;
-  const int h = blockIdx.x - rank * HV;
+  const int rank = blockIdx.x / (HV * PARTS);
+  const int hp = blockIdx.x - rank * (HV * PARTS);
+  const int h = hp / PARTS;
+  const int cb = (hp - h * PARTS) * NCOL;   // the part's first value column
   const int hk = h / (HV / HK);
-  const int n_seqs = gridDim.x / HV;
+  const int n_seqs = gridDim.x / (HV * PARTS);
   const int r = lpt_sequence<kChainThreads>(cu, n_seqs, rank, tid);
 
   const int64_t slot = ids[r];
@@ -403,11 +431,11 @@ __global__ void __launch_bounds__(kChainThreads, 2) chunk_chain_kernel(
         tma_load_2d(kq0 + blk * 16384 + ilv_row(32 * hf, true) * 128, &tm_q, hk * kD + blk * 64,
                     (int)(start + c * kC + 32 * hf), b);
   };
-  auto load_v = [&](int c) {
+  auto load_v = [&](int c) {        // the part's value columns
     const uint32_t b = smem_u32(&sm.lbar[2]);
-    mbar_expect_tx(b, 2 * 8192);
-    for (int blk = 0; blk < 2; ++blk)
-      tma_load_2d(smem_u32(sm.v[blk]), &tm_v, h * kD + blk * 64, (int)(start + c * kC), b);
+    mbar_expect_tx(b, NB * 8192);
+    for (int blk = 0; blk < NB; ++blk)
+      tma_load_2d(smem_u32(sm.v[blk]), &tm_v, h * kD + cb + blk * 64, (int)(start + c * kC), b);
   };
   auto load_tile = [&](int c) {     // the [T; M2] tile of chunk c's block
     const uint32_t b = smem_u32(&sm.lbar[3]);
@@ -437,14 +465,16 @@ __global__ void __launch_bounds__(kChainThreads, 2) chunk_chain_kernel(
     load_v(0);
   }
   uint32_t lphase[5] = {0u, 0u, 0u, 0u, 0u};
-  if (warp == 0) tmem_alloc(smem_u32(&sm.tmem_base), 256);
+  constexpr uint32_t kTmemCols = 2 * NCOL;
+  if (warp == 0) tmem_alloc(smem_u32(&sm.tmem_base), kTmemCols);
   fence_before();
   __syncthreads();
   fence_after();
   const uint32_t tbase = sm.tmem_base;
   const uint32_t tl = tbase + ((uint32_t)(qd * 32) << 16);   // this warp's lane window
-  constexpr uint32_t kColS = 0, kColW = 128;
-  const uint32_t c0 = (uint32_t)half * 64;                  // this warp's column half
+  constexpr uint32_t kColS = 0, kColW = NCOL;
+  const uint32_t c0 = (uint32_t)half * CPT;                 // this warp's columns in the part
+  const uint32_t blk0 = c0 >> 6, cin = c0 & 63;              // their 64-column block, offset
   uint32_t phase = 0;
 
   // One thread waits on each barrier; the others wait at the CTA barrier
@@ -473,10 +503,10 @@ __global__ void __launch_bounds__(kChainThreads, 2) chunk_chain_kernel(
     fence_after();
   };
 
-  // initial state -> TMEM (thread: dk row `row`, dv columns [c0, c0 + 64))
-  float* sp = pool + slot * slot_stride + (int64_t)h * kD * kD + (int64_t)row * kD + c0;
+  // initial state -> TMEM (thread: dk row `row`, value columns cb + c0 + [0, CPT))
+  float* sp = pool + slot * slot_stride + (int64_t)h * kD * kD + (int64_t)row * kD + cb + c0;
 #pragma unroll
-  for (int cg = 0; cg < 2; ++cg) {
+  for (int cg = 0; cg < CG; ++cg) {
     float s[32];
     const float4* src = reinterpret_cast<const float4*>(sp + cg * 32);
 #pragma unroll
@@ -490,9 +520,10 @@ __global__ void __launch_bounds__(kChainThreads, 2) chunk_chain_kernel(
 
   const uint32_t scr0 = smem_u32(sm.scratch);
   const uint32_t a40 = smem_u32(sm.a4);
-  constexpr uint32_t kLoOff = 16384;                 // R / W lo tiles after the hi tiles
-  uint8_t* whi = sm.scratch + half * 8192;           // this warp's dv block of R / W
+  constexpr uint32_t kLoOff = NB * 8192;             // R / W lo tiles after the hi tiles
+  uint8_t* whi = sm.scratch + blk0 * 8192;           // this warp's dv block of R / W
   uint8_t* wlo = whi + kLoOff;
+  constexpr uint32_t kIdesc = idesc_bf16(128, NCOL, false, true);
   bool ok = true;
 
   for (int c = 0; c < nchunks && ok; ++c) {
@@ -520,13 +551,13 @@ __global__ void __launch_bounds__(kChainThreads, 2) chunk_chain_kernel(
     // S (state after the previous chunk) -> bf16 MN-major tile (row = dk,
     // col = dv) for MMA 3; then S *= e^gamma_L in TMEM for MMA 5
     {
-      float s[2][32];
-      tmem_ld32x2(tl + kColS + c0, tl + kColS + c0 + 32, s[0], s[1]);
+      float s[CG][32];
+      tmem_ld_groups<CG>(tl + kColS + c0, s);
 #pragma unroll
-      for (int cg = 0; cg < 2; ++cg) {
+      for (int cg = 0; cg < CG; ++cg) {
 #pragma unroll
         for (int q8 = 0; q8 < 4; ++q8)
-          st8(sm.scratch + half * 16384, row, cg * 32 + q8 * 8, s[cg] + q8 * 8);
+          st8(sm.scratch + blk0 * 16384, row, cin + cg * 32 + q8 * 8, s[cg] + q8 * 8);
 #pragma unroll
         for (int e = 0; e < 32; e += 2)
           fmul2(s[cg][e], s[cg][e + 1], s[cg][e], s[cg][e + 1], egl, egl);
@@ -550,13 +581,13 @@ __global__ void __launch_bounds__(kChainThreads, 2) chunk_chain_kernel(
     sync_for_mma();
     if (sm.abort) { ok = false; break; }
 
-    // ---- (3) XQ = [K; Q] S : M=128, N=128, K=128 (dk); B = S rows (MN-major)
+    // ---- (3) XQ = [K; Q] S : M=128, N=NCOL, K=128 (dk); B = S rows (MN-major)
     if (tid == 0) {
 #pragma unroll
       for (int s = 0; s < 8; ++s)
         mma_bf16(tbase + kColW,
                  smem_desc(kq0 + (uint32_t)(s >> 2) * 16384u + (uint32_t)(s & 3) * 32u, 16, 1024),
-                 smem_desc(scr0 + s * 2048, 16384, 1024), idesc_bf16(128, 128, false, true), s > 0);
+                 smem_desc(scr0 + s * 2048, 16384, 1024), kIdesc, s > 0);
       mma_commit(bar);
     }
     if (tid == 0) {
@@ -571,37 +602,33 @@ __global__ void __launch_bounds__(kChainThreads, 2) chunk_chain_kernel(
 
     // ---- R = beta (v - e^gamma nk X) -> hi / lo tiles (K rows), those TMEM rows cleared;
     // Q rows: QS *= e^gamma nq in TMEM (fp32)
-    if (second) {
-      float x[2][32];
-      tmem_ld32x2(tl + kColW + c0, tl + kColW + c0 + 32, x[0], x[1]);
+    {
+      float xx[CG][32];
+      tmem_ld_groups<CG>(tl + kColW + c0, xx);
 #pragma unroll
-      for (int cg = 0; cg < 2; ++cg) {
-#pragma unroll
-        for (int e = 0; e < 32; e += 2)
-          fmul2(x[cg][e], x[cg][e + 1], x[cg][e], x[cg][e + 1], f0, f0);
-        tmem_st32(tl + kColW + c0 + cg * 32, x[cg]);
-      }
-    } else {
-      float xx[2][32];
-      tmem_ld32x2(tl + kColW + c0, tl + kColW + c0 + 32, xx[0], xx[1]);
-#pragma unroll
-      for (int cg = 0; cg < 2; ++cg) {
+      for (int cg = 0; cg < CG; ++cg) {
         float (&x)[32] = xx[cg];
+        if (second) {
 #pragma unroll
-        for (int q8 = 0; q8 < 4; ++q8) {
-          float vv[8], rr[8];
-          const int chk = cg * 4 + q8;               // 16-byte chunk within the dv block
-          unpack8(i < nv ? *reinterpret_cast<const uint4*>(sm.v[half] + sw128(i, chk * 8))
-                         : make_uint4(0, 0, 0, 0), vv);
+          for (int e = 0; e < 32; e += 2) fmul2(x[e], x[e + 1], x[e], x[e + 1], f0, f0);
+        } else {
 #pragma unroll
-          for (int e = 0; e < 8; e += 2) {
-            ffma2(rr[e], rr[e + 1], -f0, -f0, x[q8 * 8 + e], x[q8 * 8 + e + 1], vv[e], vv[e + 1]);
-            fmul2(rr[e], rr[e + 1], rr[e], rr[e + 1], bi, bi);
+          for (int q8 = 0; q8 < 4; ++q8) {
+            float vv[8], rr[8];
+            const uint32_t col = cin + cg * 32 + q8 * 8;   // column within the dv block
+            unpack8(i < nv ? *reinterpret_cast<const uint4*>(sm.v[blk0] + sw128(i, col))
+                           : make_uint4(0, 0, 0, 0), vv);
+#pragma unroll
+            for (int e = 0; e < 8; e += 2) {
+              ffma2(rr[e], rr[e + 1], -f0, -f0, x[q8 * 8 + e], x[q8 * 8 + e + 1], vv[e],
+                    vv[e + 1]);
+              fmul2(rr[e], rr[e + 1], rr[e], rr[e + 1], bi, bi);
+            }
+            split8(rr, whi, wlo, sw128(i, col));
           }
-          split8(rr, whi, wlo, sw128(i, chk * 8));
-        }
 #pragma unroll
-        for (int e = 0; e < 32; ++e) x[e] = 0.f;
+          for (int e = 0; e < 32; ++e) x[e] = 0.f;
+        }
         tmem_st32(tl + kColW + c0 + cg * 32, x);
       }
     }
@@ -616,8 +643,8 @@ __global__ void __launch_bounds__(kChainThreads, 2) chunk_chain_kernel(
 #pragma unroll
       for (int s = 0; s < 8; ++s)
         mma_bf16(tbase + kColW, smem_desc(a40 + (s & 3) * 32, 16, 1024),
-                 smem_desc((s < 4 ? scr0 : scr0 + kLoOff) + (s & 3) * 2048, 8192, 1024),
-                 idesc_bf16(128, 128, false, true), 1u);
+                 smem_desc((s < 4 ? scr0 : scr0 + kLoOff) + (s & 3) * 2048, 8192, 1024), kIdesc,
+                 1u);
       mma_commit(bar);
     }
     if (!(ok = wait_mma())) break;
@@ -625,47 +652,47 @@ __global__ void __launch_bounds__(kChainThreads, 2) chunk_chain_kernel(
     // ---- epilogue: W = nk e^(gamma_L-gamma) v' (T rows); out (M2 rows) -> bf16
     // tile in the (consumed) a4 buffer, stored by TMA while MMA 5 runs
     {
-      float vv[2][32];
-      tmem_ld32x2(tl + kColW + c0, tl + kColW + c0 + 32, vv[0], vv[1]);
+      float vv[CG][32];
+      tmem_ld_groups<CG>(tl + kColW + c0, vv);
       if (!second) {
 #pragma unroll
-        for (int cg = 0; cg < 2; ++cg) {
+        for (int cg = 0; cg < CG; ++cg) {
 #pragma unroll
           for (int q8 = 0; q8 < 4; ++q8) {
             float x[8];
 #pragma unroll
             for (int e = 0; e < 8; e += 2)
               fmul2(x[e], x[e + 1], wk, wk, vv[cg][q8 * 8 + e], vv[cg][q8 * 8 + e + 1]);
-            split8(x, whi, wlo, sw128(i, cg * 32 + q8 * 8));
+            split8(x, whi, wlo, sw128(i, cin + cg * 32 + q8 * 8));
           }
         }
       } else if (full || i < nv) {
 #pragma unroll
-        for (int cg = 0; cg < 2; ++cg)
+        for (int cg = 0; cg < CG; ++cg)
 #pragma unroll
           for (int q8 = 0; q8 < 4; ++q8) {
             if (full) {
-              st8(sm.a4 + half * 8192, i, cg * 32 + q8 * 8, vv[cg] + q8 * 8);
+              st8(sm.a4 + blk0 * 8192, i, cin + cg * 32 + q8 * 8, vv[cg] + q8 * 8);
             } else {   // a partial last chunk: rows past the end belong to the next sequence
-              *reinterpret_cast<uint4*>(out + ((t0 + i) * HV + h) * kD + c0 + cg * 32 + q8 * 8) =
-                  pack8(vv[cg] + q8 * 8);
+              *reinterpret_cast<uint4*>(out + ((t0 + i) * HV + h) * kD + cb + c0 + cg * 32 +
+                                        q8 * 8) = pack8(vv[cg] + q8 * 8);
             }
           }
       }
     }
     sync_for_mma();
 
-    // ---- (5) S += K^T [W_hi;W_lo] : M=128 (dk), N=128, K=64+64; A = K^T (MN-major)
+    // ---- (5) S += K^T [W_hi;W_lo] : M=128 (dk), N=NCOL, K=64+64; A = K^T (MN-major)
     if (tid == 0) {
 #pragma unroll
       for (int s = 0; s < 8; ++s)
         mma_bf16(tbase + kColS, smem_desc(kq0 + ilv_row(16 * (s & 3), false) * 128, 16384, 1024),
                  smem_desc((s < 4 ? scr0 : scr0 + kLoOff) + (s & 3) * 2048, 8192, 1024),
-                 idesc_bf16(128, 128, true, true), 1u);
+                 idesc_bf16(128, NCOL, true, true), 1u);
       mma_commit(bar);
       if (full) {
-        for (int blk = 0; blk < 2; ++blk)
-          tma_store_2d(&tm_out, h * kD + blk * 64, (int)t0, a40 + blk * 8192);
+        for (int blk = 0; blk < NB; ++blk)
+          tma_store_2d(&tm_out, h * kD + cb + blk * 64, (int)t0, a40 + blk * 8192);
         bulk_commit();
       }
     }
@@ -679,7 +706,7 @@ __global__ void __launch_bounds__(kChainThreads, 2) chunk_chain_kernel(
   if (tid == 0) bulk_wait_all();   // out tiles written before the CTA leaves
   if (ok) {   // final state -> pool slot
 #pragma unroll
-    for (int cg = 0; cg < 2; ++cg) {
+    for (int cg = 0; cg < CG; ++cg) {
       float s[32];
       tmem_ld32(tl + kColS + c0 + cg * 32, s);
       float4* dst = reinterpret_cast<float4*>(sp + cg * 32);
@@ -691,7 +718,7 @@ __global__ void __launch_bounds__(kChainThreads, 2) chunk_chain_kernel(
   fence_before();
   __syncthreads();
   fence_after();
-  if (warp == 0) tmem_dealloc(tbase, 256);
+  if (warp == 0) tmem_dealloc(tbase, kTmemCols);
 }
 
 }  // namespace wy
@@ -732,12 +759,22 @@ int chunk_prefill_wy(int n_seqs, int HV, cudaStream_t s, const bf16* q, int64_t 
   int2* chunk_info = reinterpret_cast<int2*>(ws + align256((n_seqs + 1) * 4));
   uint8_t* blocks = ws + align256((n_seqs + 1) * 4) + align256(cap * 8);
   const size_t prep_smem = sizeof(wy::PrepSmem) + 1024;
-  const size_t chain_smem = sizeof(wy::ChainSmem) + 1024;
+  // Column parts: with fewer chains than two per SM (a long-context prefill
+  // of a few sequences) each chain's state is split into two 64-column parts,
+  // which halves the per-chunk work on the serial path of each CTA.
+  const int64_t chains = (int64_t)n_seqs * HV;
+  const bool split_cols = chains < 2 * (int64_t)sm_count();
+  const size_t chain_smem =
+      (split_cols ? sizeof(wy::ChainSmem<64>) : sizeof(wy::ChainSmem<128>)) + 1024;
   cudaError_t e = cudaFuncSetAttribute(wy::chunk_prep_kernel,
                                        cudaFuncAttributeMaxDynamicSharedMemorySize, (int)prep_smem);
   if (e == cudaSuccess)
-    e = cudaFuncSetAttribute(wy::chunk_chain_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             (int)chain_smem);
+    e = split_cols ? cudaFuncSetAttribute(wy::chunk_chain_kernel<64>,
+                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          (int)chain_smem)
+                   : cudaFuncSetAttribute(wy::chunk_chain_kernel<128>,
+                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          (int)chain_smem);
   if (e != cudaSuccess) {
     set_error("gdn_chunk_prefill_varlen: cudaFuncSetAttribute failed: %s", cudaGetErrorString(e));
     return GDN_ERR_CUDA;
@@ -749,10 +786,14 @@ int chunk_prefill_wy(int n_seqs, int HV, cudaStream_t s, const bf16* q, int64_t 
   wy::chunk_prep_kernel<<<(unsigned)(cap * ((HV + 1) / 2)), wy::kPrepThreads, prep_smem, s>>>(
       tm_q, tm_k, g, beta, chunk_info, HK, HV, scale, blocks, status);
   if ((rc = check_launch("gdn_chunk_prefill_varlen")) != GDN_OK) return rc;
-  wy::chunk_chain_kernel<<<(unsigned)((int64_t)n_seqs * HV), wy::kChainThreads, chain_smem, s>>>(
-      tm_q32, tm_k32, tm_v, tm_out, blocks, chunk_start, pool, slot_stride, num_slots, ids, cu,
-      n_tokens,
-      max_seqlen, out, HK, HV, status);
+  if (split_cols)
+    wy::chunk_chain_kernel<64><<<(unsigned)(chains * 2), wy::kChainThreads, chain_smem, s>>>(
+        tm_q32, tm_k32, tm_v, tm_out, blocks, chunk_start, pool, slot_stride, num_slots, ids, cu,
+        n_tokens, max_seqlen, out, HK, HV, status);
+  else
+    wy::chunk_chain_kernel<128><<<(unsigned)chains, wy::kChainThreads, chain_smem, s>>>(
+        tm_q32, tm_k32, tm_v, tm_out, blocks, chunk_start, pool, slot_stride, num_slots, ids, cu,
+        n_tokens, max_seqlen, out, HK, HV, status);
   return check_launch("gdn_chunk_prefill_varlen");
 }
 

@@ -2,6 +2,8 @@
 #include <stdarg.h>
 #include <stdio.h>
 
+#include <atomic>
+
 #include "common.cuh"
 #include "tmap.cuh"
 
@@ -53,8 +55,19 @@ int sm_count() {
   return cached[dev];
 }
 
+static std::atomic<int64_t> g_wait_limit{-1};
+
+uint32_t wait_limit(uint32_t dflt) {
+  const int64_t v = g_wait_limit.load(std::memory_order_relaxed);
+  return v < 0 ? dflt : (uint32_t)(v > 0xFFFFFFFFll ? 0xFFFFFFFFll : v);
+}
+
 }  // namespace gdn
 
 extern "C" int gdn_abi_version(void) { return GDN_ABI_VERSION; }
+
+extern "C" void gdn_set_wait_limit(int64_t polls) {
+  gdn::g_wait_limit.store(polls < 0 ? -1 : polls, std::memory_order_relaxed);
+}
 
 extern "C" const char* gdn_last_error(void) { return gdn::g_last_error; }

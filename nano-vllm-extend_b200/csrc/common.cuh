@@ -21,6 +21,10 @@ int check_launch(const char* what);
 // Number of SMs of the current device (cached per device).
 int sm_count();
 
+// Poll limit for the bounded device waits that honour gdn_set_wait_limit():
+// `dflt` unless a test has set an override.
+uint32_t wait_limit(uint32_t dflt);
+
 // Gated RMSNorm launch (gate_norm.cu); x and y may alias (in place).
 int launch_rms_norm_gated(const void* x, const void* gate, int64_t gate_token_stride,
                           int heads_per_token, const void* weight, void* y, int64_t n_rows,

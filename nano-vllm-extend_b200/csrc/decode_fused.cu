@@ -37,6 +37,8 @@
 // returns.
 #include <algorithm>
 
+#include <mutex>
+
 #include "common.cuh"
 #include "tc_util.cuh"
 #include "tmap.cuh"
@@ -519,7 +521,7 @@ __global__ void __launch_bounds__(HeadCfg<D>::NT) decode_head_kernel(
     float* __restrict__ pool, int64_t slot_stride, int64_t num_slots,
     const int64_t* __restrict__ ids, const bf16* __restrict__ nw, float eps,
     bf16* __restrict__ out, int HK, int R, float scale, int32_t* __restrict__ group_cnt,
-    int32_t* status) {
+    int32_t* status, uint32_t state_spin) {
   constexpr int NT = HeadCfg<D>::NT;
   constexpr int CG = D / 4;         // threads across a state row (float4 each)
   constexpr int RG = NT / CG;       // rows per pass
@@ -637,8 +639,9 @@ __global__ void __launch_bounds__(HeadCfg<D>::NT) decode_head_kernel(
   const float eg = expf(sm.gate_g);
   const float bt = sm.gate_b;
 
-  // ---- the state has arrived (bounded wait) ----
-  if (!tc::mbar_wait(bar, 0, kDecSpin)) {
+  // ---- the state has arrived (bounded wait; state_spin polls, kDecSpin unless a
+  // test lowered it through gdn_set_wait_limit) ----
+  if (!tc::mbar_wait(bar, 0, state_spin)) {
     sm.abort = 1;
     if (status) atomicOr(status, GDN_STATUS_TIMEOUT);
   }
@@ -730,7 +733,8 @@ static int launch_decode_head(int64_t units, cudaStream_t s, const bf16* mixed, 
   }
   decode_head_kernel<D, K><<<(unsigned)units, HeadCfg<D>::NT, smem, s>>>(
       mixed, ms, z, zs, b, a, abs_, conv_pool, conv_ss, conv_w, a_log, dt_bias, param_f32, pool,
-      slot_stride, num_slots, ids, nw, eps, out, HK, R, scale, group_cnt, status);
+      slot_stride, num_slots, ids, nw, eps, out, HK, R, scale, group_cnt, status,
+      wait_limit(kDecSpin));
   return check_launch("gdn_decode_fused");
 }
 
@@ -889,13 +893,19 @@ namespace gdn {
 constexpr int64_t kStaticMaxGroups = 16384;   // bs * num_k_heads, 64 KiB of counters
 static __device__ __align__(256) int32_t g_static_group_counters[kStaticMaxGroups];
 
+// The lookup is serialised by a mutex (concurrent first calls from several host
+// threads are safe).  The address is that of the module's array in the context
+// current at the first call on the device, which is the device's primary
+// context for a runtime-API caller; a later cudaDeviceReset invalidates it.
 static int32_t* static_group_counters() {
   static int32_t* ptr[64] = {nullptr};
+  static std::mutex mu;
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
     set_error("gdn_decode_fused_static: no current CUDA device (or device index >= 64)");
     return nullptr;
   }
+  std::lock_guard<std::mutex> lock(mu);
   if (ptr[dev] == nullptr) {
     void* p = nullptr;
     const cudaError_t e = cudaGetSymbolAddress(&p, g_static_group_counters);

@@ -60,6 +60,11 @@ class Qwen3_5GatedDeltaNet(nn.Module):
     # B200 (bs 1..256).  False runs the four operators (identical results
     # wherever their recurrent kernel runs full tiles).
     fused_decode = True
+    # Publish the kernels' device status word to pinned host memory after each
+    # call (one 4-byte asynchronous copy) and raise at the next call if a
+    # kernel flagged a fault (bad slot id, malformed cu_seqlens, a wait that
+    # gave up).  See ops.poll_status for graph-replayed steps.
+    report_status = True
 
     def __init__(self, config, parallel=None, get_context=None) -> None:
         super().__init__()
@@ -151,6 +156,8 @@ class Qwen3_5GatedDeltaNet(nn.Module):
         assert self.s_cache is not None and self.conv_cache is not None, \
             "state pools not bound (s_cache / conv_cache)"
         assert hidden_states.dtype == torch.bfloat16, "the GDN kernels take bf16 activations"
+        if self.report_status:
+            ops.poll_status(hidden_states.device)      # faults of earlier calls raise here
         ctx = self._get_context()
         ids = ctx.linear_state_ids
         N = hidden_states.shape[0]
@@ -186,6 +193,8 @@ class Qwen3_5GatedDeltaNet(nn.Module):
                                        self.dt_bias[self._v_head_slice], None)
             self._prefill_core(mixed[n1:], g, beta, ids[n1:], cu_p, max(lens_q[n1:]), z[n1:],
                                out=core[n1:])
+        if self.report_status:
+            ops.publish_status(hidden_states.device)
         return self.out_proj(core.view(N, vd))
 
     def _split(self, y: torch.Tensor):

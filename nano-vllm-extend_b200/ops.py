@@ -10,8 +10,16 @@ scatters pool rows around a kernel, these operators take the pool view and the
 slot ids and update the slots in place.
 
 Slot-id faults never touch memory: the kernels skip such rows and raise a bit
-in a per-device status word; :func:`check_status` reads and clears it (it
-synchronises, so call it in tests and debug paths, not every step).
+in a per-device status word.  Two ways read it:
+
+* :func:`check_status` synchronises, reads and clears it (tests, debug paths);
+* :func:`publish_status` enqueues an asynchronous copy of the word into pinned
+  host memory on the current stream (capturable: a CUDA graph replays it), and
+  :func:`poll_status` reads that host copy without synchronising and raises if
+  a bit is set.  The layer publishes after each call and polls before the
+  next, so a fault raises at the latest one step after the kernels that saw
+  it have run; an engine that replays whole decode steps from a CUDA graph
+  calls :func:`poll_status` between steps.
 """
 from __future__ import annotations
 
@@ -40,13 +48,7 @@ def status_word(device) -> torch.Tensor:
     return t
 
 
-def check_status(device=None, clear: bool = True) -> int:
-    """Read (and clear) the status word; raise if a kernel flagged a fault."""
-    device = device if device is not None else torch.device("cuda", torch.cuda.current_device())
-    st = status_word(device)
-    v = int(st.item())
-    if clear:
-        st.zero_()
+def _raise_for(v: int) -> int:
     if v & _lib.GDN_STATUS_BAD_SLOT:
         raise IndexError(f"GDN kernel saw a slot id outside the pool (status {v:#x})")
     if v & _lib.GDN_STATUS_TIMEOUT:
@@ -54,6 +56,66 @@ def check_status(device=None, clear: bool = True) -> int:
     if v & _lib.GDN_STATUS_BAD_SEQLEN:
         raise ValueError(f"GDN kernel saw malformed cu_seqlens / max_seqlen (status {v:#x})")
     return v
+
+
+def check_status(device=None, clear: bool = True) -> int:
+    """Read (and clear) the status word; raise if a kernel flagged a fault.
+    Synchronises with the device."""
+    device = device if device is not None else torch.device("cuda", torch.cuda.current_device())
+    st = status_word(device)
+    v = int(st.item())
+    if clear:
+        st.zero_()
+        h = _HOST_STATUS.get(st.device.index)
+        if h is not None:
+            h.zero_()
+    return _raise_for(v)
+
+
+_HOST_STATUS: dict[int, torch.Tensor] = {}
+
+
+def _host_status(idx: int) -> torch.Tensor:
+    t = _HOST_STATUS.get(idx)
+    if t is None:
+        with torch.inference_mode(False):
+            t = torch.zeros(1, dtype=torch.int32).pin_memory()
+        _HOST_STATUS[idx] = t
+    return t
+
+
+def publish_status(device) -> None:
+    """Enqueue a copy of the device status word into this device's pinned host
+    mirror on the current stream (no synchronisation; recorded into a CUDA
+    graph when called under capture)."""
+    st = status_word(device)
+    _host_status(st.device.index).copy_(st, non_blocking=True)
+
+
+def poll_status(device=None) -> int:
+    """Raise if the pinned host mirror holds a fault bit (no synchronisation:
+    it reflects the last published copy that has completed).  Raising clears
+    the device word (stream-ordered) and the mirror.  Returns the mirrored
+    value (0 when clean)."""
+    device = torch.device(device) if device is not None else \
+        torch.device("cuda", torch.cuda.current_device())
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    h = _HOST_STATUS.get(idx)
+    if h is None:
+        return 0
+    v = int(h[0])
+    if v:
+        status_word(device).zero_()
+        h.zero_()
+        _raise_for(v)
+    return v
+
+
+def set_wait_limit(polls: int | None) -> None:
+    """Test hook (gdn_set_wait_limit): the poll limit of the head-per-CTA
+    decode form's bounded wait for its state copy; None restores the
+    default.  Calls made while a limit is set give invalid results."""
+    _lib.load().gdn_set_wait_limit(-1 if polls is None else int(polls))
 
 
 def _out_buffer(out, shape, device) -> torch.Tensor:
@@ -388,7 +450,11 @@ def group_counters(device, n: int) -> torch.Tensor:
     n entries; all zero between calls — the kernel leaves them zero).  Made
     outside inference mode so it is a normal tensor, 65536 entries (256 KiB)
     at first so it practically never grows; a buffer that is outgrown stays
-    allocated, because CUDA graphs captured earlier keep its address."""
+    allocated, because CUDA graphs captured earlier keep its address.  One
+    buffer per device serves every stream (a graph captured on a side stream
+    reuses the buffer of the eager warm-up calls), so decode_fused calls on
+    one device must not run concurrently on different streams: their
+    counters would mix."""
     device = torch.device(device)
     idx = device.index if device.index is not None else torch.cuda.current_device()
     t = _COUNTERS.get(idx)

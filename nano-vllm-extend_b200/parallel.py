@@ -51,7 +51,8 @@ def init_parallel_state(rank: int, world_size: int, tp_size: int, pp_size: int):
     _tp_group = None
     for pp in range(pp_size):
         ranks = list(range(pp * tp_size, (pp + 1) * tp_size))
-        group = dist.new_group(ranks) if world_size > 1 else None
+        group = dist.new_group(ranks, timeout=make_process_group_timeout()) \
+            if world_size > 1 else None
         if pp == _pp_rank:
             _tp_group = group
     _initialized = True
@@ -194,10 +195,16 @@ class PipelineHandoff:
 
     def __init__(self, hidden_size: int, max_tokens: int, dtype: torch.dtype,
                  device: torch.device, peer_prev: int | None, peer_next: int | None,
-                 group=None, mode: str = "packed"):
+                 group=None, mode: str = "packed", recv_group=None, send_group=None):
+        """``group`` carries both directions unless ``recv_group`` /
+        ``send_group`` (e.g. a two-rank group per stage boundary, so one
+        boundary's messages never queue behind another's) are given.  Peers
+        are global ranks."""
         assert mode in ("packed", "presum")
         self.H, self.max_tokens, self.dtype, self.device = hidden_size, max_tokens, dtype, device
         self.prev, self.next, self.group, self.mode = peer_prev, peer_next, group, mode
+        self.recv_group = recv_group if recv_group is not None else group
+        self.send_group = send_group if send_group is not None else group
         self.parts = 2 if mode == "packed" else 1
         # flat buffers: a message of n tokens is the contiguous prefix viewed
         # as [parts, n, H], so each part is itself a contiguous [n, H] tensor
@@ -236,9 +243,9 @@ class PipelineHandoff:
             ev.record(torch.cuda.current_stream(self.device))
             with torch.cuda.stream(self.stream):
                 self.stream.wait_event(ev)
-                self._send_work[i] = dist.isend(buf, self.next, group=self.group)
+                self._send_work[i] = dist.isend(buf, self.next, group=self.send_group)
         else:
-            self._send_work[i] = dist.isend(buf, self.next, group=self.group)
+            self._send_work[i] = dist.isend(buf, self.next, group=self.send_group)
 
     def recv(self, n: int):
         """Receive the previous stage's message for ``n`` tokens; returns
@@ -255,13 +262,13 @@ class PipelineHandoff:
             ev0.record(cur)          # earlier readers of this buffer are done
             with torch.cuda.stream(self.stream):
                 self.stream.wait_event(ev0)
-                w = dist.irecv(buf, self.prev, group=self.group)
+                w = dist.irecv(buf, self.prev, group=self.recv_group)
                 w.wait()             # orders the comm stream, not the host
                 ev = torch.cuda.Event()
                 ev.record(self.stream)
             cur.wait_event(ev)
         else:
-            dist.irecv(buf, self.prev, group=self.group).wait()
+            dist.irecv(buf, self.prev, group=self.recv_group).wait()
         if self.mode == "packed":
             return buf[0], buf[1]
         return buf[0], None
@@ -270,6 +277,14 @@ class PipelineHandoff:
         """Wait for every outstanding send (call before tearing down)."""
         for i in range(2):
             self._wait_send(i)
+
+
+def boundary_groups(world_size: int):
+    """One two-rank process group per pipeline boundary (stage b -> b + 1),
+    created in the same order on every rank (new_group is collective over
+    the default group).  Returns the list indexed by boundary."""
+    return [dist.new_group([b, b + 1], timeout=make_process_group_timeout())
+            for b in range(world_size - 1)]
 
 
 def make_process_group_timeout(seconds: float = 60.0) -> timedelta:

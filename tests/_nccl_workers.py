@@ -68,7 +68,7 @@ def _run(pkg, m, h, ids, lens):
         ctx.reset_context()
 
 
-def tp_layer_worker(rank, world, port, D):
+def tp_layer_worker(rank, world, port, D, HK=4, HV=8):
     """V-head sharded layer on `world` GPUs (TP group over NCCL): prefill of
     three sequences then decode steps; every rank's all-reduced output equals
     the unsharded layer run on the same GPU, and each rank's state slots hold
@@ -78,7 +78,7 @@ def tp_layer_worker(rank, world, port, D):
     P = pkg.parallel
     P.init_parallel_state(rank, world, tp_size=world, pp_size=1)
     dev = torch.device("cuda", rank)
-    hidden, HK, HV, K = 512, 4, 8, 4
+    hidden, K = 512, 4
     cfg = _cfg(hidden, HK, HV, D, K)
     W = I.layer_weights(hidden, HK, D, HV, D, K, seed=21)
     m = _build(pkg, cfg, W, dev)                                     # this rank's shard

@@ -110,3 +110,35 @@ def layer_pools(slots, HV, DK, DV, conv_dim, K, seed=16):
     s = (r.standard_normal((slots, 1, HV, DK, DV)) * 0.02).astype(np.float32)
     conv = _round_bf16(r.standard_normal((slots, 1, conv_dim, K - 1)).astype(np.float32))
     return s, conv
+
+
+# a two-layer decoder stack at config-0 shapes (both layers linear attention)
+DEC = dict(layers=2, inter=1024, slots=6, ids=(5, 1, 3, 0))
+
+
+def decoder_weights(hidden, inter, HK, DK, HV, DV, K, layers=2, seed=60):
+    """Parameters of a stack of Qwen3.5 decoder layers whose token mixer is the
+    GDN layer: {"<layer>.<parameter name>": array}, names as the reference's
+    Qwen3_5DecoderLayer (linear_attn.*, mlp.*, *_layernorm.weight)."""
+    out = {}
+    gdn_names = dict(in_proj_qkv="linear_attn.in_proj_qkv.weight",
+                     in_proj_z="linear_attn.in_proj_z.weight",
+                     in_proj_b="linear_attn.in_proj_b.weight",
+                     in_proj_a="linear_attn.in_proj_a.weight",
+                     conv1d="linear_attn.conv1d.weight", A_log="linear_attn.A_log",
+                     dt_bias="linear_attn.dt_bias", norm="linear_attn.norm.weight",
+                     out_proj="linear_attn.out_proj.weight")
+    for i in range(layers):
+        W = layer_weights(hidden, HK, DK, HV, DV, K, seed=seed + i)
+        for k, name in gdn_names.items():
+            out[f"{i}.{name}"] = W[k]
+        r = rng(seed + 100 + i)
+        out[f"{i}.mlp.gate_up_proj.weight"] = (
+            r.standard_normal((2 * inter, hidden), dtype=np.float32) * hidden ** -0.5)
+        out[f"{i}.mlp.down_proj.weight"] = (
+            r.standard_normal((hidden, inter), dtype=np.float32) * inter ** -0.5)
+        # Gemma-style norms: the weight is applied as (1 + w)
+        out[f"{i}.input_layernorm.weight"] = r.standard_normal(hidden, dtype=np.float32) * 0.1
+        out[f"{i}.post_attention_layernorm.weight"] = (
+            r.standard_normal(hidden, dtype=np.float32) * 0.1)
+    return out

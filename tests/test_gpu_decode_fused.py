@@ -208,3 +208,43 @@ def test_decode_fused_bad_slot_is_flagged_not_touched(ops, counters):
     assert np.array_equal(s_got[keep], c["s_pool"][keep])
     assert np.array_equal(cv_got[keep], c["conv_pool"][keep])
     assert not np.array_equal(s_got[1], c["s_pool"][1])
+
+
+def test_decode_wait_that_runs_out_sets_timeout_and_returns(ops):
+    """A bounded device wait that runs out: with the poll limit of the
+    head-per-CTA form's wait for its state copy lowered to 0 (the test hook
+    gdn_set_wait_limit), every CTA gives up at once, ORs GDN_STATUS_TIMEOUT,
+    waits (normal limit) for the copy it has in flight and returns without
+    writing any recurrent state.  The group counters stay zero, the context
+    stays usable, and the next call with the normal limit matches the oracle
+    (from the conv state the timed-out call left: its conv step had run)."""
+    HK, HV, D, K, bs = 2, 4, 128, 4, 5
+    c = make_case(HK, HV, D, K, bs, seed=971)
+    ops.check_status()
+    proj_d = dev(c["proj"], torch.bfloat16)
+    mixed, z, b, a = views(c, proj_d)
+    s_d, cv_d = dev(c["s_pool"]), dev(c["conv_pool"], torch.bfloat16)
+    L, ids = c["layer"], torch.as_tensor(c["ids"], device=DEV)
+    args = (cv_d[:, L], dev(c["conv_w"], torch.bfloat16), dev(c["a_log"]), dev(c["dt_bias"]),
+            s_d[:, L], ids, dev(c["norm_w"], torch.bfloat16), 1e-6)
+    ops.set_wait_limit(0)
+    try:
+        ops.decode_fused(mixed, z, b, a, *args, counters=True)
+        torch.cuda.synchronize()
+    finally:
+        ops.set_wait_limit(None)
+    with pytest.raises(ops._lib.GdnError):
+        ops.check_status()
+    assert counters_zero(ops)
+    assert np.array_equal(host(s_d), c["s_pool"])          # no state was written
+    cv_after = host(cv_d)
+    out = ops.decode_fused(mixed, z, b, a, *args, counters=True)
+    ops.check_status()
+    s_ref, cv_ref = c["s_pool"].copy(), cv_after.copy()
+    C, p = c["C"], c["proj"]
+    ref = O.gdn_core_decode(p[:, :C], p[:, C + HV * D + HV:C + HV * D + 2 * HV],
+                            p[:, C + HV * D:C + HV * D + HV], p[:, C:C + HV * D],
+                            cv_ref[:, L], s_ref[:, L], c["ids"], c["conv_w"], c["a_log"],
+                            c["dt_bias"], c["norm_w"], HK, D, HV, D)
+    assert np.abs(host(out).reshape(bs, -1) - ref).max() <= OUT_ATOL
+    assert state_rel(host(s_d)[c["ids"], L], s_ref[c["ids"], L]) <= STATE_RTOL

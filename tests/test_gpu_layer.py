@@ -210,3 +210,23 @@ def test_install_swaps_the_class(L):
     assert seen.get("called")
     L.layer.uninstall(prev, Q)
     assert Q.Qwen3_5GatedDeltaNet is object
+
+
+def test_layer_bad_slot_raises_at_the_next_call(L):
+    """A bad slot id in one forward call is flagged on the device, published
+    to pinned host memory after the call, and raised (IndexError) by the next
+    forward call once the first has run; the call after that is clean."""
+    c = I.C0
+    W = I.layer_weights(c["hidden"], c["HK"], c["DK"], c["HV"], c["DV"], c["K"], seed=12)
+    m = build_layer(L, cfg_c0(), W)
+    m.s_cache = torch.zeros(4, c["HV"], c["DK"], c["DV"], device=DEV)
+    m.conv_cache = torch.zeros(4, m.conv_dim, c["K"] - 1, dtype=torch.bfloat16, device=DEV)
+    L.ops.check_status()
+    run(L, m, I.layer_hidden(2, c["hidden"], seed=1), [0, 9], [1, 1])    # slot 9 is outside
+    torch.cuda.synchronize()            # the step has run (an engine syncs to sample)
+    with pytest.raises(IndexError):
+        run(L, m, I.layer_hidden(2, c["hidden"], seed=2), [0, 1], [1, 1])
+    run(L, m, I.layer_hidden(2, c["hidden"], seed=3), [0, 1], [1, 1])
+    torch.cuda.synchronize()
+    assert L.ops.poll_status() == 0
+    L.ops.check_status()

@@ -20,7 +20,7 @@ def _port():
     return p
 
 
-def _run(target, *args, world=2, timeout=240):
+def _run(target, *args, world=2, timeout=300):
     ctx = mp.get_context("spawn")
     port = _port()
     procs = [ctx.Process(target=target, args=(r, world, port) + args) for r in range(world)]
@@ -67,3 +67,16 @@ def test_tp4_head_sharded_layer_nccl(D):
 def test_pipeline_handoff_nccl_4_stages(mode):
     _need(4)
     assert _run(W.nccl_handoff_worker, mode, world=4) == [0, 0, 0, 0]
+
+
+@pytest.mark.parametrize("D", [128, 64])
+def test_tp8_head_sharded_layer_nccl(D):
+    """Eight TP ranks: one k-head and two v-heads each (16 v-heads total)."""
+    _need(8)
+    assert _run(W.tp_layer_worker, D, 8, 16, world=8) == [0] * 8
+
+
+@pytest.mark.parametrize("mode", ["packed", "presum"])
+def test_pipeline_handoff_nccl_8_stages(mode):
+    _need(8)
+    assert _run(W.nccl_handoff_worker, mode, world=8) == [0] * 8

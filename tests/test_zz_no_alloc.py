@@ -1,11 +1,13 @@
 """gdn_decode_fused_static — the fused decode core with its group counters in a
 static device array instead of caller scratch — against gdn_decode_fused with
-caller scratch, both through the C ABI: two calls in a row on the same pools,
-outputs within the path's bf16 tolerance, states within the fp32 state
-tolerance, conv-state rolls bit-exact.  Batches that fit one wave use the
-counters; the larger one runs the persistent form.  Self-contained, so it
-passes alone and after every other test (the static counters start and end
-at zero)."""
+caller scratch, both through the C ABI: three calls in a row on the same
+pools, each with a different permutation of slot ids, so a counter left
+non-zero by one call would change which CTA rolls the shared q/k conv taps of
+the next.  Both entry points run the same kernels, so outputs, states and
+conv-state rolls must agree bit for bit (which also meets the path's bf16 and
+fp32 tolerances).  Batches that fit one wave use the counters; the larger one
+runs the persistent form.  Self-contained, so it passes alone and after every
+other test (the static counters start and end at zero)."""
 import ctypes
 
 import numpy as np
@@ -33,11 +35,11 @@ def _dev(a, dtype=torch.float32):
     return torch.from_numpy(np.array(a, np.float32, order="C", copy=True)).to(DEV).to(dtype)
 
 
-def _case(HK, HV, D, K, bs, seed):
+def _case(HK, HV, D, K, bs, seed, calls=3):
     r = I.rng(seed)
     C = (2 * HK + HV) * D
     W = C + HV * D + 2 * HV + 8
-    projs = [O.round_bf16(r.standard_normal((bs, W)).astype(np.float32)) for _ in range(2)]
+    projs = [O.round_bf16(r.standard_normal((bs, W)).astype(np.float32)) for _ in range(calls)]
     slots = bs + 3
     s_pool = (r.standard_normal((slots, 2, HV, D, D)) * 0.02).astype(np.float32)
     conv_pool = O.round_bf16(r.standard_normal((slots, 2, C, K - 1)).astype(np.float32))
@@ -45,7 +47,7 @@ def _case(HK, HV, D, K, bs, seed):
     a_log = r.uniform(-1.0, 1.0, HV).astype(np.float32)
     dt_bias = r.uniform(-0.5, 0.5, HV).astype(np.float32)
     norm_w = O.round_bf16((1 + 0.1 * r.standard_normal(D)).astype(np.float32))
-    ids = r.permutation(slots)[:bs]
+    ids = [r.permutation(slots)[:bs] for _ in range(calls)]   # new slot ids every call
     return C, projs, s_pool, conv_pool, conv_w, a_log, dt_bias, norm_w, ids
 
 
@@ -71,18 +73,18 @@ def _run_static(pkg, proj, C, HK, HV, D, K, cv, w, al, dt, sp, ids, nw, out):
     (2, 8, 64, 3, 20),       # four v-heads per k-head share the counters, head dim 64
     (16, 32, 128, 4, 64),    # 2048 units: several waves, the persistent form
 ])
-def test_static_scratch_equals_caller_scratch_two_calls(lib, HK, HV, D, K, bs):
+def test_static_scratch_equals_caller_scratch_three_calls(lib, HK, HV, D, K, bs):
     C, projs, s_pool, conv_pool, conv_w, a_log, dt_bias, norm_w, ids = _case(HK, HV, D, K, bs,
                                                                              seed=1200 + bs)
     ops = lib.ops
     w = _dev(conv_w, torch.bfloat16)
     al, dt = _dev(a_log), _dev(dt_bias)
     nw = _dev(norm_w, torch.bfloat16)
-    ids_d = torch.as_tensor(ids, device=DEV, dtype=torch.int64)
     s_a, s_b = _dev(s_pool), _dev(s_pool)
     c_a, c_b = _dev(conv_pool, torch.bfloat16), _dev(conv_pool, torch.bfloat16)
-    for step in range(2):                       # two calls in a row thread both states
+    for step in range(len(projs)):              # calls in a row thread both states
         proj = _dev(projs[step], torch.bfloat16)
+        ids_d = torch.as_tensor(ids[step], device=DEV, dtype=torch.int64)
         ref = ops.decode_fused(proj[:, :C], proj[:, C:C + HV * D].view(bs, HV, D),
                                proj[:, C + HV * D:C + HV * D + HV],
                                proj[:, C + HV * D + HV:C + HV * D + 2 * HV], c_a[:, 1], w, al,
@@ -91,9 +93,11 @@ def test_static_scratch_equals_caller_scratch_two_calls(lib, HK, HV, D, K, bs):
         _run_static(lib, proj, C, HK, HV, D, K, c_b[:, 1], w, al, dt, s_b[:, 1], ids_d, nw, got)
         torch.cuda.synchronize()
         assert (got.float() - ref.float()).abs().max().item() <= OUT_ATOL, f"call {step}"
-        assert torch.equal(c_a, c_b), f"call {step}: conv state"
         rel = ((s_a - s_b).norm() / s_a.norm()).item()
         assert rel <= STATE_RTOL, f"call {step}: state rel {rel}"
+        assert torch.equal(got, ref), f"call {step}: outputs differ"
+        assert torch.equal(s_a, s_b), f"call {step}: states differ"
+        assert torch.equal(c_a, c_b), f"call {step}: conv state"
     ops.check_status()
 
 
