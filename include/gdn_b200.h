@@ -38,7 +38,7 @@
 extern "C" {
 #endif
 
-#define GDN_ABI_VERSION 5
+#define GDN_ABI_VERSION 6
 
 enum gdn_status_code {
   GDN_OK = 0,
