@@ -371,10 +371,13 @@ def pp_bench(pkg, dev, world, rank, steps, warmup):
     P = pkg.parallel
     lo, hi = P.split_layers(c["layers"], world, rank)
     prev, nxt = P.pp_peers(rank, 1, world)
-    groups = P.boundary_groups(world)
     stage = HybridStage(pkg, dev, seed=4321 + rank, lo=lo, hi=hi, first=prev is None,
                         last=nxt is None)
     stage.capture()
+    barrier(world)
+    # the boundary groups are made after every rank's capture: no NCCL communicator
+    # is created or connected while a CUDA graph is being captured
+    groups = P.boundary_groups(world)
     ho = P.PipelineHandoff(c["hidden"], c["bs"], torch.bfloat16, dev, prev, nxt, mode="packed",
                            recv_group=groups[rank - 1] if prev is not None else None,
                            send_group=groups[rank] if nxt is not None else None)
@@ -914,6 +917,10 @@ def config4_bench(pkg, dev, world, rank, peaks):
     prefill()
     cu1 = torch.arange(n + 1, dtype=torch.int32, device=dev)
     h = torch.randn(n, c["hidden"], generator=g, device=dev).to(torch.bfloat16)
+    # the captured step holds no NCCL call: out_proj's all-reduce of the [8, 2048]
+    # partial sums is timed on its own below
+    tp_size = m.out_proj.tp_size
+    m.out_proj.tp_size = 1
     ctx.set_context(cu1, cu1, 1, 1, linear_state_ids=ids)
     try:
         with torch.inference_mode():
@@ -925,9 +932,17 @@ def config4_bench(pkg, dev, world, rank, peaks):
                 yd = m(None, h)
     finally:
         ctx.reset_context()
+        m.out_proj.tp_size = tp_size
     steps = c4["decode_steps"]
     t_dec = time_region(graph.replay, steps, world) / steps
     del graph
+    t_ar = 0.0
+    if world > 1:
+        yr = torch.empty(n, c["hidden"], dtype=torch.bfloat16, device=dev)
+        for _ in range(5):
+            torch.distributed.all_reduce(yr, group=m.out_proj.tp_group)
+        t_ar = time_region(lambda: torch.distributed.all_reduce(yr, group=m.out_proj.tp_group),
+                           200, world) / 200
     # the fused decode core alone (the kernel the decode step runs), CUDA events
     bs, HK, HV, D = n, m.num_k_heads, m.num_v_heads, c["DK"]
     pj = torch.randn(bs, m._fused_weight().shape[0], generator=g, device=dev).to(torch.bfloat16)
@@ -962,8 +977,10 @@ def config4_bench(pkg, dev, world, rank, peaks):
                        "chunk_tflops": round(flops / t_chunk / 1e12, 2),
                        "chunk_frac_of_bf16_peak": round(flops / t_chunk / 1e12 /
                                                         peaks["bf16_tflops"], 4)},
-           "decode": {"steps": steps, "ms_per_step": round(t_dec * 1e3, 4),
-                      "tok_s": round(n / t_dec, 1),
+           "decode": {"steps": steps, "ms_per_step": round((t_dec + t_ar) * 1e3, 4),
+                      "tok_s": round(n / (t_dec + t_ar), 1),
+                      "ms_per_step_layer_graph": round(t_dec * 1e3, 4),
+                      "ms_allreduce_per_step": round(t_ar * 1e3, 4),
                       "core_kernel_us": round(t_core * 1e6, 2),
                       "core_state_gbs": round(state_bytes / t_core / 1e9, 1),
                       "core_achieved_gbs": round(dec_bytes / t_core / 1e9, 1),
