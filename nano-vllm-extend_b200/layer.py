@@ -24,6 +24,8 @@ What differs is the execution, B200-first:
 """
 from __future__ import annotations
 
+import contextlib
+
 import torch
 import torch.nn.functional as F
 from torch import nn
@@ -65,6 +67,10 @@ class Qwen3_5GatedDeltaNet(nn.Module):
     # kernel flagged a fault (bad slot id, malformed cu_seqlens, a wait that
     # gave up).  See ops.poll_status for graph-replayed steps.
     report_status = True
+    # Mark the layer's phases with NVTX ranges ("gdn.in_proj", "gdn.decode_core",
+    # "gdn.gate", "gdn.conv", "gdn.chunk", "gdn.out_proj") for nsys-style
+    # timelines; off by default (a range costs a host call per phase).
+    nvtx = False
 
     def __init__(self, config, parallel=None, get_context=None) -> None:
         super().__init__()
@@ -150,6 +156,9 @@ class Qwen3_5GatedDeltaNet(nn.Module):
 
     # -- forward --------------------------------------------------------------
 
+    def _range(self, name: str):
+        return torch.cuda.nvtx.range(name) if self.nvtx else contextlib.nullcontext()
+
     def forward(self, positions: torch.Tensor, hidden_states: torch.Tensor) -> torch.Tensor:
         """hidden_states [N, hidden] (varlen concatenation, decode rows
         first) -> [N, hidden]; slot states updated in place."""
@@ -164,7 +173,8 @@ class Qwen3_5GatedDeltaNet(nn.Module):
         cd, vd, hv = self.conv_dim, self.value_dim, self.num_v_heads
         r = self._proj_rows
 
-        proj = F.linear(hidden_states, self._fused_weight())        # [N, total]
+        with self._range("gdn.in_proj"):
+            proj = F.linear(hidden_states, self._fused_weight())    # [N, total]
         mixed = proj[:, :cd]
         z = proj[:, r[0]:r[1]].view(N, hv, self.head_v_dim)
         b = proj[:, r[1]:r[2]]
@@ -185,17 +195,20 @@ class Qwen3_5GatedDeltaNet(nn.Module):
         core = torch.empty(N, hv, self.head_v_dim, dtype=torch.bfloat16,
                            device=hidden_states.device)
         if n1:
-            self._decode_core(mixed[:n1], z[:n1], b[:n1], a[:n1], ids[:n1], out=core[:n1])
+            with self._range("gdn.decode_core"):
+                self._decode_core(mixed[:n1], z[:n1], b[:n1], a[:n1], ids[:n1], out=core[:n1])
         if n1 < N:
             cu_q = ctx.cu_seqlens_q
             cu_p = cu_q[n1:] - cu_q[n1] if n1 else cu_q
-            g, beta = ops.fused_g_beta(b[n1:], a[n1:], self.A_log[self._v_head_slice],
-                                       self.dt_bias[self._v_head_slice], None)
+            with self._range("gdn.gate"):
+                g, beta = ops.fused_g_beta(b[n1:], a[n1:], self.A_log[self._v_head_slice],
+                                           self.dt_bias[self._v_head_slice], None)
             self._prefill_core(mixed[n1:], g, beta, ids[n1:], cu_p, max(lens_q[n1:]), z[n1:],
                                out=core[n1:])
         if self.report_status:
             ops.publish_status(hidden_states.device)
-        return self.out_proj(core.view(N, vd))
+        with self._range("gdn.out_proj"):
+            return self.out_proj(core.view(N, vd))
 
     def _split(self, y: torch.Tensor):
         kd = self.key_dim
@@ -230,13 +243,15 @@ class Qwen3_5GatedDeltaNet(nn.Module):
     def _prefill_core(self, mixed, g, beta, ids, cu_seqlens, max_seqlen, z, out=None):
         """Prefill rows: varlen conv + chunked rule with slot states + gated
         norm (the composition of qwen3_5.py:922-963, unpadded)."""
-        y = ops.causal_conv_silu_varlen(mixed, self.conv_cache, ids,
-                                        self.conv1d.weight.view(self.conv_dim, self.conv_kernel),
-                                        cu_seqlens)
+        with self._range("gdn.conv"):
+            y = ops.causal_conv_silu_varlen(
+                mixed, self.conv_cache, ids,
+                self.conv1d.weight.view(self.conv_dim, self.conv_kernel), cu_seqlens)
         q, k, v = self._split(y)
-        return ops.chunk_gated_delta_rule_varlen(q, k, v, g, beta, self.s_cache, ids, cu_seqlens,
-                                                 max_seqlen, z=z, norm_weight=self.norm.weight,
-                                                 eps=self.norm.eps, out=out)
+        with self._range("gdn.chunk"):
+            return ops.chunk_gated_delta_rule_varlen(
+                q, k, v, g, beta, self.s_cache, ids, cu_seqlens, max_seqlen, z=z,
+                norm_weight=self.norm.weight, eps=self.norm.eps, out=out)
 
 
 def install(qwen3_5_module=None, parallel_module=None, context_module=None):

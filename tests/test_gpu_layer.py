@@ -230,3 +230,20 @@ def test_layer_bad_slot_raises_at_the_next_call(L):
     torch.cuda.synchronize()
     assert L.ops.poll_status() == 0
     L.ops.check_status()
+
+
+def test_layer_nvtx_ranges_leave_results_unchanged(L):
+    """With the NVTX ranges on, a prefill + decode gives the same bits."""
+    c = I.C0
+    W = I.layer_weights(c["hidden"], c["HK"], c["DK"], c["HV"], c["DV"], c["K"], seed=14)
+    outs = []
+    for nv in (False, True):
+        m = build_layer(L, cfg_c0(), W)
+        m.nvtx = nv
+        m.s_cache = torch.zeros(4, c["HV"], c["DK"], c["DV"], device=DEV)
+        m.conv_cache = torch.zeros(4, m.conv_dim, c["K"] - 1, dtype=torch.bfloat16, device=DEV)
+        y0 = run(L, m, I.layer_hidden(70, c["hidden"], seed=5), [2, 0], [40, 30])
+        y1 = run(L, m, I.layer_hidden(2, c["hidden"], seed=6), [2, 0], [1, 1])
+        outs.append((y0, y1, m.s_cache.clone()))
+    for a, b in zip(*outs):
+        assert torch.equal(a, b)
