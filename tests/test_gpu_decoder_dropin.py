@@ -15,10 +15,13 @@ norm helpers run eagerly here (dynamo disabled for the test), and its
 flashinfer norms are switched off, as in the golden run.
 
 Tolerances (layer-level bf16: the projections and MLPs are different bf16
-GEMMs on the two sides, CPU torch against cuBLAS, and a one-ulp flip of a
-bf16 activation of magnitude 2-4 is 0.016): hidden outputs and the residual
-stream within 2e-2 plus one bf16 ulp of the value; final recurrent states
-relative <= 2e-2; conv states (raw projection outputs) within one bf16 ulp.
+GEMMs on the two sides, CPU torch against cuBLAS; a one-ulp flip of a bf16
+activation of magnitude 2-4 is 0.016, and the residual stream is a chain of
+four bf16 sums whose terms may each differ by an ulp): hidden outputs and the
+residual stream within 2e-2 plus two bf16 ulps of the value per element and
+a mean absolute error <= 5e-3 (a wiring fault gives errors of order one);
+final recurrent states relative <= 2e-2; conv states (raw projection
+outputs) within one bf16 ulp.
 """
 import os
 import sys
@@ -118,10 +121,11 @@ def test_installed_layer_in_reference_decoder_stack(pkg, ref_modules, golden_dir
                                                   for s in range(len(dec))]
     for step, ((h, r), (h_ref, r_ref)) in enumerate(zip(got, refs)):
         h, r = h.float().cpu().numpy(), r.float().cpu().numpy()
-        eh = np.abs(h - h_ref) - _bf16_ulp(h_ref)
-        assert eh.max() <= 2e-2, f"step {step}: hidden beyond 2e-2 + 1 ulp by {eh.max()}"
-        er = np.abs(r - r_ref) - _bf16_ulp(r_ref)
-        assert er.max() <= 2e-2, f"step {step}: residual beyond 2e-2 + 1 ulp by {er.max()}"
+        for name, x, x_ref in (("hidden", h, h_ref), ("residual", r, r_ref)):
+            d = np.abs(x - x_ref)
+            e = d - 2 * _bf16_ulp(x_ref)
+            assert e.max() <= 2e-2, f"step {step}: {name} beyond 2e-2 + 2 ulps by {e.max()}"
+            assert d.mean() <= 5e-3, f"step {step}: {name} mean |error| {d.mean()}"
     rel = np.linalg.norm(s_rows - d["s_rows"]) / np.linalg.norm(d["s_rows"])
     assert rel <= 2e-2, f"state rel {rel}"
     ec = np.abs(conv_rows - d["conv_rows"]) - _bf16_ulp(d["conv_rows"])
