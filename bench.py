@@ -48,6 +48,14 @@ C2 = dict(n_seqs=64, len_lo=128, len_hi=8192, hidden=2048, HK=16, DK=128, HV=32,
 CHUNK_FLOPS_PER_TOKEN_HEAD = 180_224   # 4C*Dk + 2C*Dk + 4C*Dv + 6*Dk*Dv at C=64, Dk=Dv=128
 
 
+class OneRank:
+    """Parallel state of an unsharded layer (tp size 1), passed explicitly to
+    every layer that must not pick up the package's process-wide TP state."""
+    get_tp_rank = staticmethod(lambda: 0)
+    get_tp_size = staticmethod(lambda: 1)
+    get_tp_group = staticmethod(lambda: None)
+
+
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -169,7 +177,8 @@ class DecodeStack:
         torch.set_default_dtype(torch.bfloat16)
         try:
             with torch.device(device), torch.no_grad():
-                self.layers = [pkg.layer.Qwen3_5GatedDeltaNet(cfg) for _ in range(n_layers)]
+                self.layers = [pkg.layer.Qwen3_5GatedDeltaNet(cfg, parallel=OneRank)
+                               for _ in range(n_layers)]
                 for m in self.layers:
                     h = c["hidden"]
                     Fw = m._fused_weight()
@@ -279,7 +288,8 @@ class HybridStage:
                     L["v_cache"] = nrm(bs, c["kv_heads"], self.ctx_len, c["head_dim"], std=1.0)
                 else:
                     with torch.device(dev), torch.no_grad():
-                        m = pkg.layer.Qwen3_5GatedDeltaNet(cfg)
+                        # unsharded: a pipeline stage's layers hold no collective
+                        m = pkg.layer.Qwen3_5GatedDeltaNet(cfg, parallel=OneRank)
                         m._fused_weight().normal_(0, H ** -0.5, generator=g)
                         m.conv1d.weight.uniform_(-0.5, 0.5, generator=g)
                         m.A_log.uniform_(-1.0, 0.0, generator=g)
@@ -556,7 +566,7 @@ def prefill_bench(pkg, device, steps, peaks):
     torch.set_default_dtype(torch.bfloat16)
     try:
         with torch.device(device), torch.no_grad():
-            m = pkg.layer.Qwen3_5GatedDeltaNet(cfg)
+            m = pkg.layer.Qwen3_5GatedDeltaNet(cfg, parallel=OneRank)
             m._fused_weight().normal_(0, c["hidden"] ** -0.5, generator=g)
             m.conv1d.weight.uniform_(-0.5, 0.5, generator=g)
             m.A_log.uniform_(-1.0, 0.0, generator=g)
@@ -764,10 +774,7 @@ def tp_prefill_bench(pkg, dev, world, rank, steps):
     cfg = config2_cfg()
     W = config2_full_weights(dev, seed=11)
     m = build_loaded_layer(pkg, cfg, W, dev)                      # this rank's shard
-    one = type("OneRank", (), dict(get_tp_rank=staticmethod(lambda: 0),
-                                   get_tp_size=staticmethod(lambda: 1),
-                                   get_tp_group=staticmethod(lambda: None)))
-    ref = build_loaded_layer(pkg, cfg, W, dev, parallel=one)      # the whole layer
+    ref = build_loaded_layer(pkg, cfg, W, dev, parallel=OneRank)  # the whole layer
     del W
     pools = pkg.state_pool.StatePools([m], c["n_seqs"], dev)
     ref_pools = pkg.state_pool.StatePools([ref], c["n_seqs"], dev)
@@ -835,6 +842,7 @@ def tp_prefill_bench(pkg, dev, world, rank, steps):
                          "pass": bool(out_err <= 2e-2 and state_rel <= 2e-2)}}
     del m, ref, pools, ref_pools, x, y_tp, y_ref
     torch.cuda.empty_cache()
+    P.reset_parallel_state()     # later sections build unsharded layers
     return res
 
 
@@ -990,6 +998,7 @@ def config4_bench(pkg, dev, world, rank, peaks):
                               "the launch is latency-bound, far from the HBM roofline"}}
     del m, pools, x, pj
     torch.cuda.empty_cache()
+    P.reset_parallel_state()
     return res
 
 
