@@ -411,6 +411,7 @@ def pp_bench(pkg, dev, world, rank, steps, warmup):
             h, r = ho.recv(c["bs"])
             stage.x_h.copy_(h)
             stage.x_r.copy_(r)
+            ho.consumed()        # the next receive need not wait for this step's compute
         stage.replay()
         if nxt is not None:
             ho.send(stage.y_h, stage.y_r)

@@ -215,6 +215,8 @@ class PipelineHandoff:
         self._send_work = [None, None]
         self._slot = 0
         self._rslot = 0
+        self._recv_free = [None, None]   # per receive buffer: its readers are done
+        self._last_recv = None
         self.cuda = device.type == "cuda"
         self.stream = torch.cuda.Stream(device=device) if self.cuda else None
 
@@ -258,8 +260,11 @@ class PipelineHandoff:
         buf = self._recv[i][:self.parts * n * self.H].view(self.parts, n, self.H)
         if self.cuda:
             cur = torch.cuda.current_stream(self.device)
-            ev0 = torch.cuda.Event()
-            ev0.record(cur)          # earlier readers of this buffer are done
+            ev0 = self._recv_free[i]
+            if ev0 is None:          # no consumed() mark: wait for all the stream has queued
+                ev0 = torch.cuda.Event()
+                ev0.record(cur)
+            self._recv_free[i] = None
             with torch.cuda.stream(self.stream):
                 self.stream.wait_event(ev0)
                 w = dist.irecv(buf, self.prev, group=self.recv_group)
@@ -269,9 +274,23 @@ class PipelineHandoff:
             cur.wait_event(ev)
         else:
             dist.irecv(buf, self.prev, group=self.recv_group).wait()
+        self._last_recv = i
         if self.mode == "packed":
             return buf[0], buf[1]
         return buf[0], None
+
+    def consumed(self):
+        """Mark the tensors of the last recv() as read by the work queued so far
+        on the current stream (e.g. after copying them into the stage's input).
+        The next receive into that buffer then waits only for those reads, not
+        for everything the stream queued later (the stage's own compute), so the
+        transfer overlaps the compute.  Optional: without it a receive waits for
+        all work queued before it."""
+        if self.cuda and self._last_recv is not None:
+            ev = torch.cuda.Event()
+            ev.record(torch.cuda.current_stream(self.device))
+            self._recv_free[self._last_recv] = ev
+        self._last_recv = None
 
     def flush(self):
         """Wait for every outstanding send (call before tearing down)."""

@@ -110,13 +110,19 @@ def tp_layer_worker(rank, world, port, D, HK=4, HV=8):
 
 def nccl_handoff_worker(rank, world, port, mode):
     """PipelineHandoff between consecutive GPUs over NCCL on the side stream:
-    several steps in flight (double buffers), receiver ordered on events."""
+    several steps in flight (double buffers), receiver ordered on events; the
+    packed mode on per-boundary process groups, presum on the default group."""
     pkg = _init(rank, world, port)
     P = pkg.parallel
     dev = torch.device("cuda", rank)
     H, N = 2048, 64
     prev, nxt = P.pp_peers(rank, 1, world)
-    ho = P.PipelineHandoff(H, 256, torch.bfloat16, dev, prev, nxt, mode=mode)
+    kw = {}
+    if mode == "packed":        # one two-rank group per boundary; presum uses the default group
+        groups = P.boundary_groups(world)
+        kw = dict(recv_group=groups[rank - 1] if prev is not None else None,
+                  send_group=groups[rank] if nxt is not None else None)
+    ho = P.PipelineHandoff(H, 256, torch.bfloat16, dev, prev, nxt, mode=mode, **kw)
     g = torch.Generator(device=dev).manual_seed(0)
     steps = []
     for s in range(6):
@@ -127,8 +133,15 @@ def nccl_handoff_worker(rank, world, port, mode):
         for h, r in steps:
             ho.send(h, r)
     if prev is not None:
+        # receive every step before checking any: each message is copied out and
+        # marked consumed(), so a later receive into the same (double) buffer
+        # waits only for that copy; an early overwrite would corrupt a copy
+        got = []
         for h, r in steps:
             hh, rr = ho.recv(h.shape[0])
+            got.append((hh.clone(), None if rr is None else rr.clone()))
+            ho.consumed()
+        for (h, r), (hh, rr) in zip(steps, got):
             if mode == "packed":
                 assert torch.equal(hh, h) and torch.equal(rr, r)
             else:
