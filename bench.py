@@ -982,7 +982,9 @@ def config4_bench(pkg, dev, world, rank, peaks):
                           "without the cross-shard all-reduce"),
            "prefill": {"ms": round(t_pre * 1e3, 3), "tok_s": round(N / t_pre, 1),
                        "chunk_kernels_ms": round(t_chunk * 1e3, 3),
-                       "chunk_chain_column_parts": 2 if n * HV < 2 * 148 else 1,
+                       "chunk_chain_column_parts":
+                           2 if n * m.num_v_heads < 2 * torch.cuda.get_device_properties(
+                               dev).multi_processor_count else 1,
                        "chunk_tflops": round(flops / t_chunk / 1e12, 2),
                        "chunk_frac_of_bf16_peak": round(flops / t_chunk / 1e12 /
                                                         peaks["bf16_tflops"], 4)},
@@ -995,8 +997,9 @@ def config4_bench(pkg, dev, world, rank, peaks):
                       "core_achieved_gbs": round(dec_bytes / t_core / 1e9, 1),
                       "core_frac_of_hbm": round(dec_bytes / t_core / 1e9 / peaks["hbm_gbs"], 4),
                       "algorithmic_bytes_per_launch": dec_bytes,
-                      "note": "32 (sequence, v-head) units per GPU: one 64 KiB state each; "
-                              "the launch is latency-bound, far from the HBM roofline"}}
+                      "note": f"{bs * HV} (sequence, v-head) units per GPU, one 64 KiB state "
+                              "each: a launch this small is latency-bound, far from the HBM "
+                              "roofline"}}
     del m, pools, x, pj
     torch.cuda.empty_cache()
     P.reset_parallel_state()
