@@ -68,7 +68,7 @@ def parse():
     ap.add_argument("--prefill-steps", type=int, default=3)
     ap.add_argument("--profile-case", default=None,
                     choices=["recurrent", "decode_fused", "conv_decode", "conv_varlen", "chunk",
-                             "gbeta", "norm"],
+                             "chunk_long", "gbeta", "norm"],
                     help="run a small single-kernel case for ncu (3 launches) and exit")
     return ap.parse_args()
 
@@ -1203,6 +1203,20 @@ def profile_case(pkg, name):
         w = torch.randn(C, 4, generator=g, device=dev).to(torch.bfloat16)
         ids = torch.arange(n, device=dev)
         fn = lambda: ops.conv_decode_step(x, pool, ids, w)
+    elif name == "chunk_long":         # few long chains: the chain splits into column parts
+        HKl, HVl, T = 2, 4, 16384
+        lens = [T, T]
+        N = sum(lens)
+        cu = torch.tensor([0, T, N], dtype=torch.int32, device=dev)
+        ids = torch.arange(2, device=dev)
+        x = torch.randn(N, (2 * HKl + HVl) * D, generator=g, device=dev).to(torch.bfloat16)
+        pool = torch.zeros(2, HVl, D, D, device=dev)
+        q = x[:, :HKl * D].view(N, HKl, D)
+        k = x[:, HKl * D:2 * HKl * D].view(N, HKl, D)
+        v = x[:, 2 * HKl * D:].view(N, HVl, D)
+        gg = -torch.rand(N, HVl, generator=g, device=dev)
+        beta = torch.rand(N, HVl, generator=g, device=dev).to(torch.bfloat16)
+        fn = lambda: ops.chunk_gated_delta_rule_varlen(q, k, v, gg, beta, pool, ids, cu, T)
     elif name in ("conv_varlen", "chunk", "gbeta", "norm"):
         lens = [4096] * 8 + [1000, 3000, 77, 130]
         N = sum(lens)
