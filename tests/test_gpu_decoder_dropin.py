@@ -15,13 +15,13 @@ norm helpers run eagerly here (dynamo disabled for the test), and its
 flashinfer norms are switched off, as in the golden run.
 
 Tolerances (layer-level bf16: the projections and MLPs are different bf16
-GEMMs on the two sides, CPU torch against cuBLAS; a one-ulp flip of a bf16
-activation of magnitude 2-4 is 0.016, and the residual stream is a chain of
-four bf16 sums whose terms may each differ by an ulp): hidden outputs and the
-residual stream within 2e-2 plus two bf16 ulps of the value per element and
-a mean absolute error <= 5e-3 (a wiring fault gives errors of order one);
-final recurrent states relative <= 2e-2; conv states (raw projection
-outputs) within one bf16 ulp.
+GEMMs on the two sides, CPU torch against cuBLAS; their one-ulp differences
+enter the recurrent state and compound over the 16 decode steps through two
+GDN layers and two MLPs): per step, the relative (Frobenius) error of the
+hidden outputs and of the residual stream <= 2e-2 and their largest
+element-wise error <= 5 % of the largest value (a wiring fault gives errors of
+order one); final recurrent states relative <= 2e-2; conv states (raw
+projection outputs) within one bf16 ulp.
 """
 import os
 import sys
@@ -122,10 +122,11 @@ def test_installed_layer_in_reference_decoder_stack(pkg, ref_modules, golden_dir
     for step, ((h, r), (h_ref, r_ref)) in enumerate(zip(got, refs)):
         h, r = h.float().cpu().numpy(), r.float().cpu().numpy()
         for name, x, x_ref in (("hidden", h, h_ref), ("residual", r, r_ref)):
-            d = np.abs(x - x_ref)
-            e = d - 2 * _bf16_ulp(x_ref)
-            assert e.max() <= 2e-2, f"step {step}: {name} beyond 2e-2 + 2 ulps by {e.max()}"
-            assert d.mean() <= 5e-3, f"step {step}: {name} mean |error| {d.mean()}"
+            rel = np.linalg.norm(x - x_ref) / np.linalg.norm(x_ref)
+            worst = np.abs(x - x_ref).max() / np.abs(x_ref).max()
+            print(f"step {step} {name}: relative error {rel:.2e}, max-abs / max {worst:.2e}")
+            assert rel <= 2e-2, f"step {step}: {name} relative error {rel}"
+            assert worst <= 5e-2, f"step {step}: {name} max-abs error / max value {worst}"
     rel = np.linalg.norm(s_rows - d["s_rows"]) / np.linalg.norm(d["s_rows"])
     assert rel <= 2e-2, f"state rel {rel}"
     ec = np.abs(conv_rows - d["conv_rows"]) - _bf16_ulp(d["conv_rows"])
