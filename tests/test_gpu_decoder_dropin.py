@@ -21,7 +21,8 @@ GDN layers and two MLPs): per step, the relative (Frobenius) error of the
 hidden outputs and of the residual stream <= 2e-2 and their largest
 element-wise error <= 5 % of the largest value (a wiring fault gives errors of
 order one); final recurrent states relative <= 2e-2; conv states (raw
-projection outputs) within one bf16 ulp.
+projection outputs): layer 0's, projected from the same inputs, within one
+bf16 ulp, layer 1's relative <= 2e-2.
 """
 import os
 import sys
@@ -129,5 +130,12 @@ def test_installed_layer_in_reference_decoder_stack(pkg, ref_modules, golden_dir
             assert worst <= 5e-2, f"step {step}: {name} max-abs error / max value {worst}"
     rel = np.linalg.norm(s_rows - d["s_rows"]) / np.linalg.norm(d["s_rows"])
     assert rel <= 2e-2, f"state rel {rel}"
-    ec = np.abs(conv_rows - d["conv_rows"]) - _bf16_ulp(d["conv_rows"])
-    assert ec.max() <= 1e-6, f"conv state beyond one bf16 ulp by {ec.max()}"
+    # layer 0's conv rows are projections of the same inputs on both sides (the
+    # decode steps' hidden states): one bf16 ulp; layer 1's come from layer 0's
+    # outputs, which carry the stack's bf16 drift: relative error
+    c0, c0_ref = conv_rows[:, 0], d["conv_rows"][:, 0]
+    ec = np.abs(c0 - c0_ref) - _bf16_ulp(c0_ref)
+    assert ec.max() <= 1e-6, f"layer-0 conv state beyond one bf16 ulp by {ec.max()}"
+    c1, c1_ref = conv_rows[:, 1], d["conv_rows"][:, 1]
+    rel1 = np.linalg.norm(c1 - c1_ref) / np.linalg.norm(c1_ref)
+    assert rel1 <= 2e-2, f"layer-1 conv state relative error {rel1}"
