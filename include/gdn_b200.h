@@ -265,9 +265,13 @@ int gdn_decode_fused(const void* mixed, int64_t mixed_row_stride,
  * device pointers) or that must not allocate per decode step.  The array is
  * zero when the library loads and each call leaves it zero, so it needs no
  * clearing.  The first call on a device looks its address up (with that device
- * current); make that first call before any stream capture.  Calls on one
- * device share the array: they must not overlap in time (different streams
- * running it concurrently race on the counters).
+ * current; the lookup is serialised across host threads and assumes the
+ * device's primary context); make that first call before any stream capture.
+ * Calls on one device share the array: they must not overlap in time
+ * (different streams running it concurrently race on the counters).  The
+ * size limit is the array's: only the one-wave head-per-CTA form uses the
+ * counters, and a batch that large would run the persistent form anyway, but
+ * this entry point rejects it rather than accept sizes its array cannot hold.
  */
 int gdn_decode_fused_static(const void* mixed, int64_t mixed_row_stride,
                             const void* z, int64_t z_row_stride,
