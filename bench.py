@@ -1116,6 +1116,64 @@ def cpu_baseline(budget_s=20.0):
             "sample": f"{sample}; {n} whole steps timed", "ms_per_step": round(dt * 1e3, 1)}
 
 
+def reference_torch_recurrence(budget_s=15.0):
+    """The reference's own torch decode recurrence, timed on the host cores when
+    its package is installed next to this file (baseline/_ref; None otherwise):
+    one config-1 layer step of its non-in-place decode path (qwen3_5.py:
+    1028-1030) — gather the 256 slot states from a 257-slot fp32 pool, run
+    recurrent_gated_delta_rule (the pure-torch _torch_recurrent_gated_delta_rule,
+    :616-651, with fla switched off and torch.compile disabled, run eagerly) on
+    q / k repeated to the v-heads as its split_qkv does (:1002-1005), scatter the
+    new states back.  The recurrence only (no projections, conv or norm);
+    reported per layer and scaled to the 18-layer step, labelled so."""
+    root = os.path.join(ROOT, "baseline", "_ref")
+    if not os.path.isdir(os.path.join(root, "nanovllm")):
+        return None
+    for k_, v_ in (("FLA_CHUNK", "0"), ("FLA_RECURRENT", "0"), ("NANOVLLM_FI_NORM", "0")):
+        os.environ.setdefault(k_, v_)
+    import torch._dynamo
+    sys.path.insert(0, root)
+    try:
+        import nanovllm.models.qwen3_5 as Q
+    except Exception as e:  # reported, never fatal
+        return {"unavailable": repr(e)[:200]}
+    finally:
+        sys.path.remove(root)
+    torch._dynamo.config.disable = True
+    torch.set_num_threads(os.cpu_count() or 1)
+    c = C1
+    bs, HK, HV, D = c["bs"], c["HK"], c["HV"], c["DK"]
+    g_ = torch.Generator().manual_seed(0)
+    pool = torch.randn(bs + 1, HV, D, D, generator=g_) * 0.02
+    ids = torch.randperm(bs + 1, generator=g_)[:bs]
+    q = torch.randn(bs, 1, HK, D, generator=g_).to(torch.bfloat16).repeat_interleave(2, dim=2)
+    k = torch.randn(bs, 1, HK, D, generator=g_).to(torch.bfloat16).repeat_interleave(2, dim=2)
+    v = torch.randn(bs, 1, HV, D, generator=g_).to(torch.bfloat16)
+    g = -torch.rand(bs, 1, HV, generator=g_)
+    beta = torch.rand(bs, 1, HV, generator=g_).to(torch.bfloat16)
+
+    def layer():
+        out, new_s = Q.recurrent_gated_delta_rule(q, k, v, g, beta, pool[ids])
+        pool[ids] = new_s
+        return out
+
+    with torch.inference_mode():
+        layer()
+        n, t0 = 0, time.perf_counter()
+        while n < 3 or time.perf_counter() - t0 < budget_s:
+            layer()
+            n += 1
+            if n >= 200:
+                break
+    dt = (time.perf_counter() - t0) / n
+    return {"ms_per_layer_step": round(dt * 1e3, 2),
+            "tok_s_18_layer_step": round(bs / (dt * c["layers"]), 2),
+            "threads": torch.get_num_threads(),
+            "sample": f"{n} config-1 layer steps (bs {bs}, 257-slot pool) of the reference's "
+                      "own torch recurrence with its gather / scatter, recurrence only, "
+                      "scaled x18 for the 18-layer step"}
+
+
 def decode_config(world):
     """The config dict of the decode line (both arms print the same one)."""
     c = C1
@@ -1159,6 +1217,9 @@ def run_reference(args, world, rank):
                                        f"asked), warm-up capped at 3"},
             "e2e": {"value": round(tok_s, 2), "unit": "tok/s", "h2d_bytes_per_step": 0,
                     "d2h_bytes_per_step": 0}}
+    ref_torch = reference_torch_recurrence()
+    if ref_torch is not None:
+        line["reference_torch_recurrence"] = ref_torch
     print(json.dumps(line), flush=True)
 
 
