@@ -75,6 +75,46 @@ def handoff_worker(rank, world, port, mode):
     dist.destroy_process_group()
 
 
+def handoff_chain_worker(rank, world, port):
+    """A pipeline of `world` stages on one two-rank process group per boundary
+    (boundary_groups): every stage but the first receives, adds its rank to the
+    hidden part and passes the pair on, with several steps in flight and each
+    received message copied out and marked consumed(); the last stage checks
+    that every step arrived intact through the middle stages."""
+    pkg = _init(rank, world, port)
+    P = pkg.parallel
+    H, N, steps = 32, 6, 5
+    prev, nxt = P.pp_peers(rank, 1, world)
+    groups = P.boundary_groups(world)
+    ho = P.PipelineHandoff(H, 16, torch.float32, torch.device("cpu"), prev, nxt, mode="packed",
+                           recv_group=groups[rank - 1] if prev is not None else None,
+                           send_group=groups[rank] if nxt is not None else None)
+    g = torch.Generator().manual_seed(0)
+    data = [(torch.randn(N, H, generator=g), torch.randn(N, H, generator=g))
+            for _ in range(steps)]
+    got = []
+    for s in range(steps):
+        if prev is None:
+            h, r = data[s]
+        else:
+            hh, rr = ho.recv(N)
+            h, r = hh.clone() + rank, rr.clone()
+            ho.consumed()
+        if nxt is not None:
+            ho.send(h, r)
+        else:
+            got.append((h, r))
+    ho.flush()
+    if nxt is None:
+        for (h, r), (h0, r0) in zip(got, data):
+            want = h0
+            for stage in range(1, world):      # the stages' additions, in their order
+                want = want + stage
+            assert torch.equal(h, want) and torch.equal(r, r0)
+    dist.barrier()
+    dist.destroy_process_group()
+
+
 def handoff_peer_dies_worker(rank, world, port):
     """Rank 0 leaves before sending; rank 1's receive must end with an error
     (never hang) within the short process-group timeout."""

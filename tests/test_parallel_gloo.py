@@ -1,4 +1,4 @@
-"""Multi-process (world_size 2, gloo, CPU) tests of the pipeline stage handoff,
+"""Multi-process (world_size 2 and 3, gloo, CPU) tests of the pipeline stage handoff,
 the row-parallel all-reduce, V-head sharding, and failure detection on the
 host (a peer that disappears makes the receiver error out, never hang)."""
 import multiprocessing as mp
@@ -39,6 +39,11 @@ def _run(target, *args, world=2, timeout=120, expect=0):
 @pytest.mark.parametrize("mode", ["packed", "presum"])
 def test_pipeline_handoff(mode):
     assert _run(W.handoff_worker, mode) == [0, 0]
+
+
+def test_pipeline_handoff_three_stages_boundary_groups():
+    """A middle stage receives and sends on different two-rank groups."""
+    assert _run(W.handoff_chain_worker, world=3) == [0, 0, 0]
 
 
 def test_handoff_peer_death_is_detected():
