@@ -451,6 +451,24 @@ def pp_bench(pkg, dev, world, rank, steps, warmup):
     return out
 
 
+def hybrid_single_gpu(pkg, dev, steps, warmup):
+    """The config-3-shaped hybrid decoder of pp_bench run whole on one GPU (all
+    24 layers, embedding and LM head in one CUDA graph): the step the pipeline
+    splits, for comparing pipelined throughput at N stages against one GPU."""
+    c = C3
+    stage = HybridStage(pkg, dev, seed=4321, lo=0, hi=c["layers"], first=True, last=True)
+    stage.capture()
+    for _ in range(warmup):
+        stage.replay()
+    t = time_region(stage.replay, steps, 1)
+    out = {"workload": "config3-shaped hybrid decoder (as pp), all 24 layers on one GPU, "
+                       "decode steps of 128 sequences",
+           "steps": steps, "ms_per_step": round(t / steps * 1e3, 4),
+           "tok_s": round(c["bs"] * steps / t, 1)}
+    stage.graph = None
+    return out
+
+
 def time_region(fn, steps, world, stream=None):
     """CUDA-event time of ``steps`` calls of fn, bracketed by barrier + sync."""
     barrier(world)
@@ -1392,6 +1410,11 @@ def main():
                 line["prefill"]["chunk_kernel"]["cpu_baseline"] = cpu_prefill_baseline()
         except Exception as e:  # reported, never hides the headline
             line["prefill"] = {"error": repr(e)[:300]}
+    if world == 1 and not args.no_prefill:
+        try:
+            line["hybrid_1gpu"] = hybrid_single_gpu(pkg, dev, 100, args.warmup)
+        except Exception as e:  # reported, never hides the headline
+            line["hybrid_1gpu"] = {"error": repr(e)[:300]}
     if world == 1 and not args.no_config4:
         try:
             line["config4"] = config4_bench(pkg, dev, world, rank, peaks)

@@ -66,6 +66,8 @@ struct __align__(1024) ChunkSmem {
   unsigned long long lbar[3]; // TMA loads: K, Q, V
   uint32_t tmem_base;
   int abort;
+  int issued[3];              // TMA loads issued per load barrier (K, Q, V)
+  int commits;                // MMA commits on mbar
 };
 
 __global__ void __launch_bounds__(kThreads, 2) chunk_prefill_tc_kernel(
@@ -107,6 +109,7 @@ __global__ void __launch_bounds__(kThreads, 2) chunk_prefill_tc_kernel(
   auto load_k = [&](int c) {
     if (tid == 0) {
       const uint32_t b = smem_u32(&sm.lbar[0]);
+      ++sm.issued[0];
       mbar_expect_tx(b, 2 * 8192);
       for (int blk = 0; blk < 2; ++blk)
         tma_load_2d(kq_s + blk * 16384, &tm_k, hk * kD + blk * 64, (int)(start + c * kC), b);
@@ -115,6 +118,7 @@ __global__ void __launch_bounds__(kThreads, 2) chunk_prefill_tc_kernel(
   auto load_q = [&](int c) {
     if (tid == 0) {
       const uint32_t b = smem_u32(&sm.lbar[1]);
+      ++sm.issued[1];
       mbar_expect_tx(b, 2 * 8192);
       for (int blk = 0; blk < 2; ++blk)
         tma_load_2d(kq_s + blk * 16384 + 64 * 128, &tm_q, hk * kD + blk * 64,
@@ -124,6 +128,7 @@ __global__ void __launch_bounds__(kThreads, 2) chunk_prefill_tc_kernel(
   auto load_v = [&](int c) {
     if (tid == 0) {
       const uint32_t b = smem_u32(&sm.lbar[2]);
+      ++sm.issued[2];
       mbar_expect_tx(b, 2 * 8192);
       for (int blk = 0; blk < 2; ++blk)
         tma_load_2d(smem_u32(sm.v[blk]), &tm_v, h * kD + blk * 64, (int)(start + c * kC), b);
@@ -147,9 +152,13 @@ __global__ void __launch_bounds__(kThreads, 2) chunk_prefill_tc_kernel(
   const uint32_t bar = smem_u32(&sm.mbar);
   if (tid == 0) {
     mbar_init(bar, 1);
-    for (int i = 0; i < 3; ++i) mbar_init(smem_u32(&sm.lbar[i]), 1);
+    for (int i = 0; i < 3; ++i) {
+      mbar_init(smem_u32(&sm.lbar[i]), 1);
+      sm.issued[i] = 0;
+    }
     mbar_init_fence();
     sm.abort = 0;
+    sm.commits = 0;
   }
   __syncthreads();
   load_k(0);
@@ -252,6 +261,7 @@ __global__ void __launch_bounds__(kThreads, 2) chunk_prefill_tc_kernel(
                  idesc_bf16(128, 128, false, false), s > 0);
       }
       mma_commit(bar);
+      ++sm.commits;
     }
     if (!(ok = wait_mma())) break;
     if (tid < 64) k_norm_from_diag(sm.sc, tl, kColW, tid);
@@ -277,6 +287,7 @@ __global__ void __launch_bounds__(kThreads, 2) chunk_prefill_tc_kernel(
         mma_bf16(tbase + kColW, smem_desc(qkm0 + s * 32, 16, 1024),
                  smem_desc(a40 + s * 2048, 8192, 1024), idesc_bf16(128, 64, false, true), s > 0);
       mma_commit(bar);
+      ++sm.commits;
     }
     // S (TMEM) -> bf16 MN-major tile (row = dk, col = dv); S *= e^gamma_L in TMEM
     {
@@ -315,6 +326,7 @@ __global__ void __launch_bounds__(kThreads, 2) chunk_prefill_tc_kernel(
                  smem_desc(kq0 + (uint32_t)(s >> 2) * 16384u + (uint32_t)(s & 3) * 32u, 16, 1024),
                  smem_desc(scr0 + s * 2048, 16384, 1024), idesc_bf16(128, 128, false, true), s > 0);
       mma_commit(bar);
+      ++sm.commits;
     }
     if (!(ok = wait_mma())) break;
     if (c + 1 < nchunks) load_q(c + 1);   // Q rows are no longer read this chunk
@@ -373,6 +385,7 @@ __global__ void __launch_bounds__(kThreads, 2) chunk_prefill_tc_kernel(
                  smem_desc((s < 4 ? scr0 : scr0 + kLoOff) + (s & 3) * 2048, 8192, 1024),
                  idesc_bf16(128, 128, false, true), 1u);
       mma_commit(bar);
+      ++sm.commits;
     }
     if (!(ok = wait_mma())) break;
 
@@ -419,6 +432,7 @@ __global__ void __launch_bounds__(kThreads, 2) chunk_prefill_tc_kernel(
                  smem_desc((s < 4 ? scr0 : scr0 + kLoOff) + (s & 3) * 2048, 8192, 1024),
                  idesc_bf16(128, 128, true, true), 1u);
       mma_commit(bar);
+      ++sm.commits;
     }
     if (!(ok = wait_mma())) break;
     if (c + 1 < nchunks) {            // the K rows are free: fetch the next chunk
@@ -426,9 +440,14 @@ __global__ void __launch_bounds__(kThreads, 2) chunk_prefill_tc_kernel(
       load_gb(c + 1, g_next, b_next);
     }
   }
-  if (!ok && tid == 0) {   // drain loads still in flight before the CTA exits (bounded)
+  if (!ok && tid == 0) {   // drain what is in flight before the CTA exits (bounded):
+    // loads and MMAs complete in order, so the parity of the last one issued on
+    // each barrier covers all (an already completed phase returns at once)
 #pragma unroll
-    for (int i = 0; i < 3; ++i) mbar_wait(smem_u32(&sm.lbar[i]), lphase[i], kSpin);
+    for (int i = 0; i < 3; ++i)
+      if (sm.issued[i] > 0)
+        mbar_wait(smem_u32(&sm.lbar[i]), (uint32_t)(sm.issued[i] - 1) & 1u, kSpin);
+    if (sm.commits > 0) mbar_wait(bar, (uint32_t)(sm.commits - 1) & 1u, kSpin);
   }
 
   if (ok) {   // final state -> pool slot

@@ -130,6 +130,7 @@ struct PrepSmem {             // placed at a 1024-byte aligned base (swizzle ato
   unsigned long long mbar, lbar;
   uint32_t tmem_base;
   int abort;
+  int commits;                // MMA commits on mbar
 };
 constexpr uint32_t kQkmOff = 18432;   // QKm tile (1024-aligned) after L / T (17,408 B)
 constexpr uint32_t kXOff = 26624;     // X (5 KiB) after QKm; MMA 2's unused A rows 64-127
@@ -168,6 +169,7 @@ __global__ void __launch_bounds__(kPrepThreads, kPrepCtasPerSm) chunk_prep_kerne
     mbar_init(lbar, 1);
     mbar_init_fence();
     sm.abort = 0;
+    sm.commits = 0;
     mbar_expect_tx(lbar, (own1 ? 2 : 1) * 4 * 8192);   // the boxes are issued after the barrier
   }
   if (lt < kC) {
@@ -239,6 +241,7 @@ __global__ void __launch_bounds__(kPrepThreads, kPrepCtasPerSm) chunk_prep_kerne
         }
       }
       mma_commit(bar);
+      ++sm.commits;
     }
     if (lt >= 64 && (wg == 0 || own1))          // Q rows: CUDA cores, under MMA 1
       q_norm_row(sm.sc[wg], rw, lt - 64, ilv16_row(lt - 64, true), nv, scale);
@@ -294,6 +297,7 @@ __global__ void __launch_bounds__(kPrepThreads, kPrepCtasPerSm) chunk_prep_kerne
                    idesc_bf16(128, 64, false, true), s > 0);
       }
       mma_commit(bar);
+      ++sm.commits;
     }
     ok = wait1(bar, 1);
     if (ok) {
@@ -325,6 +329,10 @@ __global__ void __launch_bounds__(kPrepThreads, kPrepCtasPerSm) chunk_prep_kerne
         bulk_wait_read();
       }
     }
+  }
+  if (sm.abort && tid == 0) {   // drain what is in flight before TMEM is freed (bounded)
+    mbar_wait(lbar, 0, kSpin);    // the one [K;Q] load batch
+    if (sm.commits > 0) mbar_wait(bar, (uint32_t)(sm.commits - 1) & 1u, kSpin);
   }
   fence_before();
   __syncthreads();
@@ -362,6 +370,8 @@ struct __align__(1024) ChainSmem {
   unsigned long long lbar[5]; // loads: K, Q, V, [T;M2] tile, factors
   uint32_t tmem_base;
   int abort;
+  int issued[5];              // loads issued per load barrier
+  int commits;                // MMA commits on mbar
 };
 
 template <int NCOL>
@@ -417,6 +427,7 @@ __global__ void __launch_bounds__(kChainThreads, 2) chunk_chain_kernel(
   // K / Q rows in 32-row boxes at their interleaved tile rows
   auto load_k = [&](int c) {
     const uint32_t b = smem_u32(&sm.lbar[0]);
+    ++sm.issued[0];
     mbar_expect_tx(b, 2 * 8192);
     for (int blk = 0; blk < 2; ++blk)
       for (int hf = 0; hf < 2; ++hf)
@@ -425,6 +436,7 @@ __global__ void __launch_bounds__(kChainThreads, 2) chunk_chain_kernel(
   };
   auto load_q = [&](int c) {
     const uint32_t b = smem_u32(&sm.lbar[1]);
+    ++sm.issued[1];
     mbar_expect_tx(b, 2 * 8192);
     for (int blk = 0; blk < 2; ++blk)
       for (int hf = 0; hf < 2; ++hf)
@@ -433,17 +445,20 @@ __global__ void __launch_bounds__(kChainThreads, 2) chunk_chain_kernel(
   };
   auto load_v = [&](int c) {        // the part's value columns
     const uint32_t b = smem_u32(&sm.lbar[2]);
+    ++sm.issued[2];
     mbar_expect_tx(b, NB * 8192);
     for (int blk = 0; blk < NB; ++blk)
       tma_load_2d(smem_u32(sm.v[blk]), &tm_v, h * kD + cb + blk * 64, (int)(start + c * kC), b);
   };
   auto load_tile = [&](int c) {     // the [T; M2] tile of chunk c's block
     const uint32_t b = smem_u32(&sm.lbar[3]);
+    ++sm.issued[3];
     mbar_expect_tx(b, kTile);
     bulk_load(smem_u32(sm.a4), blocks + ((int64_t)(cs + c) * HV + h) * kBlockBytes, kTile, b);
   };
   auto load_f = [&](int c) {        // the factors of chunk c's block, into buffer c % 2
     const uint32_t b = smem_u32(&sm.lbar[4]);
+    ++sm.issued[4];
     mbar_expect_tx(b, kScal);
     bulk_load(smem_u32(&sm.f[c & 1][0][0]),
               blocks + ((int64_t)(cs + c) * HV + h) * kBlockBytes + kTile, kScal, b);
@@ -452,9 +467,13 @@ __global__ void __launch_bounds__(kChainThreads, 2) chunk_chain_kernel(
   const uint32_t bar = smem_u32(&sm.mbar);
   if (tid == 0) {
     mbar_init(bar, 1);
-    for (int i = 0; i < 5; ++i) mbar_init(smem_u32(&sm.lbar[i]), 1);
+    for (int i = 0; i < 5; ++i) {
+      mbar_init(smem_u32(&sm.lbar[i]), 1);
+      sm.issued[i] = 0;
+    }
     mbar_init_fence();
     sm.abort = 0;
+    sm.commits = 0;
   }
   __syncthreads();
   if (tid == 0) {
@@ -589,6 +608,7 @@ __global__ void __launch_bounds__(kChainThreads, 2) chunk_chain_kernel(
                  smem_desc(kq0 + (uint32_t)(s >> 2) * 16384u + (uint32_t)(s & 3) * 32u, 16, 1024),
                  smem_desc(scr0 + s * 2048, 16384, 1024), kIdesc, s > 0);
       mma_commit(bar);
+      ++sm.commits;
     }
     if (tid == 0) {
       if (c > 0) {                 // the previous chunk's out tile has left a4: fetch [T; M2]
@@ -646,6 +666,7 @@ __global__ void __launch_bounds__(kChainThreads, 2) chunk_chain_kernel(
                  smem_desc((s < 4 ? scr0 : scr0 + kLoOff) + (s & 3) * 2048, 8192, 1024), kIdesc,
                  1u);
       mma_commit(bar);
+      ++sm.commits;
     }
     if (!(ok = wait_mma())) break;
 
@@ -690,6 +711,7 @@ __global__ void __launch_bounds__(kChainThreads, 2) chunk_chain_kernel(
                  smem_desc((s < 4 ? scr0 : scr0 + kLoOff) + (s & 3) * 2048, 8192, 1024),
                  idesc_bf16(128, NCOL, true, true), 1u);
       mma_commit(bar);
+      ++sm.commits;
       if (full) {
         for (int blk = 0; blk < NB; ++blk)
           tma_store_2d(&tm_out, h * kD + cb + blk * 64, (int)t0, a40 + blk * 8192);
@@ -699,9 +721,14 @@ __global__ void __launch_bounds__(kChainThreads, 2) chunk_chain_kernel(
     if (!(ok = wait_mma())) break;
     if (tid == kLoader && c + 1 < nchunks) load_k(c + 1);   // the K rows are free
   }
-  if (!ok && tid == 0) {   // drain loads still in flight before the CTA exits (bounded)
+  if (!ok && tid == 0) {   // drain what is in flight before the CTA exits (bounded):
+    // loads and MMAs complete in order, so the parity of the last one issued on
+    // each barrier covers all (an already completed phase returns at once)
 #pragma unroll
-    for (int i = 0; i < 5; ++i) mbar_wait(smem_u32(&sm.lbar[i]), lphase[i], kSpin);
+    for (int i = 0; i < 5; ++i)
+      if (sm.issued[i] > 0)
+        mbar_wait(smem_u32(&sm.lbar[i]), (uint32_t)(sm.issued[i] - 1) & 1u, kSpin);
+    if (sm.commits > 0) mbar_wait(bar, (uint32_t)(sm.commits - 1) & 1u, kSpin);
   }
   if (tid == 0) bulk_wait_all();   // out tiles written before the CTA leaves
   if (ok) {   // final state -> pool slot
