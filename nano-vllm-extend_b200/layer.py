@@ -62,10 +62,11 @@ class Qwen3_5GatedDeltaNet(nn.Module):
     # B200 (bs 1..256).  False runs the four operators (identical results
     # wherever their recurrent kernel runs full tiles).
     fused_decode = True
-    # Publish the kernels' device status word to pinned host memory after each
-    # call (one 4-byte asynchronous copy) and raise at the next call if a
-    # kernel flagged a fault (bad slot id, malformed cu_seqlens, a wait that
-    # gave up).  See ops.poll_status for graph-replayed steps.
+    # Poll the kernels' device status word (its pinned host copy) before each
+    # call and raise if a kernel flagged a fault (bad slot id, malformed
+    # cu_seqlens, a wait that gave up); one layer per device, the first to run,
+    # publishes the word after its kernels (one 4-byte asynchronous copy per
+    # step).  See ops.poll_status for graph-replayed steps.
     report_status = True
     # Mark the layer's phases with NVTX ranges ("gdn.in_proj", "gdn.decode_core",
     # "gdn.gate", "gdn.conv", "gdn.chunk", "gdn.out_proj") for nsys-style
@@ -205,7 +206,7 @@ class Qwen3_5GatedDeltaNet(nn.Module):
                                            self.dt_bias[self._v_head_slice], None)
             self._prefill_core(mixed[n1:], g, beta, ids[n1:], cu_p, max(lens_q[n1:]), z[n1:],
                                out=core[n1:])
-        if self.report_status:
+        if self.report_status and ops.is_status_publisher(self, hidden_states.device):
             ops.publish_status(hidden_states.device)
         with self._range("gdn.out_proj"):
             return self.out_proj(core.view(N, vd))

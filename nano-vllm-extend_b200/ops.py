@@ -16,12 +16,17 @@ in a per-device status word.  Two ways read it:
 * :func:`publish_status` enqueues an asynchronous copy of the word into pinned
   host memory on the current stream (capturable: a CUDA graph replays it), and
   :func:`poll_status` reads that host copy without synchronising and raises if
-  a bit is set.  The layer publishes after each call and polls before the
-  next, so a fault raises at the latest one step after the kernels that saw
-  it have run; an engine that replays whole decode steps from a CUDA graph
-  calls :func:`poll_status` between steps.
+  a bit is set.  Every layer polls before it runs; one layer per device (the
+  first to run, :func:`is_status_publisher`) publishes after its kernels — a
+  copy node costs ~12 us inside a decode graph, so one per step rather than
+  one per layer.  A fault is published at the latest in the step after the
+  one whose kernels saw it and raises at the next poll after that; an engine
+  that replays whole decode steps from a CUDA graph calls
+  :func:`poll_status` between steps.
 """
 from __future__ import annotations
+
+import weakref
 
 import torch
 
@@ -90,6 +95,34 @@ def publish_status(device) -> None:
     graph when called under capture)."""
     st = status_word(device)
     _host_status(st.device.index).copy_(st, non_blocking=True)
+
+
+_PUBLISHER: dict[int, weakref.ref] = {}
+
+
+def is_status_publisher(module, device) -> bool:
+    """Whether ``module`` publishes the status word of ``device``: the first
+    module to ask claims it and keeps it while it is alive (a model built later
+    claims it once the earlier one is gone)."""
+    device = torch.device(device)
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    ref = _PUBLISHER.get(idx)
+    owner = ref() if ref is not None else None
+    if owner is None:
+        _PUBLISHER[idx] = weakref.ref(module)
+        return True
+    return owner is module
+
+
+def reset_status_publisher(device=None) -> None:
+    """Forget the publishing module of ``device`` (all devices when None), so
+    the next module to run claims it."""
+    if device is None:
+        _PUBLISHER.clear()
+        return
+    device = torch.device(device)
+    _PUBLISHER.pop(device.index if device.index is not None else torch.cuda.current_device(),
+                   None)
 
 
 def poll_status(device=None) -> int:

@@ -214,11 +214,16 @@ def test_install_swaps_the_class(L):
 
 def test_layer_bad_slot_raises_at_the_next_call(L):
     """A bad slot id in one forward call is flagged on the device, published
-    to pinned host memory after the call, and raised (IndexError) by the next
-    forward call once the first has run; the call after that is clean."""
+    to pinned host memory after the call by the device's publishing layer (this
+    one), and raised (IndexError) by the next forward call once the first has
+    run; the call after that is clean.  A second layer neither publishes nor
+    takes the role while the first is alive."""
     c = I.C0
     W = I.layer_weights(c["hidden"], c["HK"], c["DK"], c["HV"], c["DV"], c["K"], seed=12)
+    L.ops.reset_status_publisher()
     m = build_layer(L, cfg_c0(), W)
+    other = build_layer(L, cfg_c0(), W)
+    assert L.ops.is_status_publisher(m, DEV) and not L.ops.is_status_publisher(other, DEV)
     m.s_cache = torch.zeros(4, c["HV"], c["DK"], c["DV"], device=DEV)
     m.conv_cache = torch.zeros(4, m.conv_dim, c["K"] - 1, dtype=torch.bfloat16, device=DEV)
     L.ops.check_status()
