@@ -439,6 +439,37 @@ def test_chunk_fused_norm(ops):
         assert_bf16_close(host(fused), host(ref), ulps=1, atol=1e-3)
 
 
+def test_chunk_fused_norm_whole_state_chains(ops):
+    """The z / norm_weight arguments on the whole-state chain form (at least
+    two chains per SM), full and partial last chunks: the result equals the
+    chunk output followed by the standalone gated norm, bit for bit."""
+    D, HK, HV = 128, 2, 4
+    sms = torch.cuda.get_device_properties(0).multi_processor_count
+    n_seqs = (2 * sms) // HV + 5
+    lens = [int(x) for x in I.rng(65).integers(1, 200, n_seqs)]
+    lens[:3] = [64, 128, 65]
+    N = sum(lens)
+    q, k, v, g, beta = I.core_inputs(N, HK, D, HV, D, seed=66)
+    q, k, v, beta = (O.round_bf16(t) for t in (q, k, v, beta))
+    r = I.rng(67)
+    zbig = O.round_bf16(r.standard_normal((N, HV * D + 8)).astype(np.float32))
+    w = O.round_bf16((1 + 0.1 * r.standard_normal(D)).astype(np.float32))
+    cu = I.cu_from_lens(lens)
+    ids = i64(np.arange(n_seqs))
+    p1 = f32((I.rng(68).standard_normal((n_seqs, HV, D, D)) * 0.02).astype(np.float32))
+    p2 = p1.clone()
+    zd = bf(zbig)[:, :HV * D].view(N, HV, D)
+    fused = ops.chunk_gated_delta_rule_varlen(bf(q), bf(k), bf(v), f32(g), bf(beta), p1, ids,
+                                              i32(cu), max(lens), z=zd, norm_weight=bf(w),
+                                              eps=1e-6)
+    plain = ops.chunk_gated_delta_rule_varlen(bf(q), bf(k), bf(v), f32(g), bf(beta), p2, ids,
+                                              i32(cu), max(lens))
+    ref = ops.rms_norm_gated(plain, zd, bf(w), 1e-6)
+    ops.check_status()
+    assert torch.equal(p1, p2)
+    assert torch.equal(fused, ref)
+
+
 # ---------------------------------------------------------------------------
 # malformed cu_seqlens: flagged on the device, never read out of bounds
 # ---------------------------------------------------------------------------
