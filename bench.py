@@ -374,6 +374,7 @@ def pp_bench(pkg, dev, world, rank, steps, warmup):
       t_local  each stage with the handoff replaced by local copies of the
                same bytes (the receive buffer copied in, the output copied out)
       t_pp     the pipeline with the NCCL handoff
+    t_local and t_pp alternate three times and their medians are used.
     K steps through S stages take K + S - 1 stage steps even with a free
     handoff (the pipeline fills once), so exposed handoff = (t_pp - fill -
     t_local) / t_pp with fill = (S - 1) t_local / K."""
@@ -416,19 +417,22 @@ def pp_bench(pkg, dev, world, rank, steps, warmup):
         if nxt is not None:
             ho.send(stage.y_h, stage.y_r)
 
-    for fn in (stage_only, local_step):
+    for fn in (stage_only, local_step, pp_step):
         for _ in range(warmup):
             fn()
+        ho.flush()
+        torch.cuda.synchronize()
     t_stage = time_region(stage_only, steps, world)
-    t_local = time_region(local_step, steps, world)
-    for _ in range(warmup):
-        pp_step()
-    ho.flush()
-    torch.cuda.synchronize()
-    t_pp = time_region(pp_step, steps, world)
-    ho.flush()
-    torch.cuda.synchronize()
+    # local-copy and pipelined timings alternate three times (medians): the GPUs'
+    # power-capped clocks drift over seconds, more than the handoff costs
+    t_locals, t_pps = [], []
+    for _ in range(3):
+        t_locals.append(time_region(local_step, steps, world))
+        t_pps.append(time_region(pp_step, steps, world))
+        ho.flush()
+        torch.cuda.synchronize()
     barrier(world)
+    t_local, t_pp = statistics.median(t_locals), statistics.median(t_pps)
     fill = (world - 1) * t_local / steps
     exposed = (t_pp - fill - t_local) / t_pp
     per_stage = [b - a for a, b in (P.split_layers(c["layers"], world, r) for r in range(world))]
@@ -442,6 +446,8 @@ def pp_bench(pkg, dev, world, rank, steps, warmup):
            "bytes_per_handoff": 2 * c["bs"] * c["hidden"] * 2, "steps": steps,
            "ms_per_step_pipelined": round(t_pp / steps * 1e3, 4),
            "ms_per_step_local_copy": round(t_local / steps * 1e3, 4),
+           "ms_per_step_runs": {"pipelined": [round(t / steps * 1e3, 4) for t in t_pps],
+                                "local_copy": [round(t / steps * 1e3, 4) for t in t_locals]},
            "ms_per_step_slowest_stage": round(t_stage / steps * 1e3, 4),
            "pipeline_fill_ms": round(fill * 1e3, 4),
            "exposed_handoff_ms_per_step": round((t_pp - fill - t_local) / steps * 1e3, 4),
