@@ -637,22 +637,20 @@ def prefill_bench(pkg, device, steps, peaks):
             proj = torch.nn.functional.linear(x, m._fused_weight())
             ev[1].record()
             r = m._proj_rows
-            gg, beta = pkg.ops.fused_g_beta(proj[:, r[1]:r[2]], proj[:, r[2]:r[3]],
-                                            m.A_log, m.dt_bias)
+            y, gg, beta = pkg.ops.conv_gate_varlen(proj[:, :m.conv_dim], m.conv_cache, ids,
+                                                   m.conv1d.weight, cu, proj[:, r[1]:r[2]],
+                                                   proj[:, r[2]:r[3]], m.A_log, m.dt_bias)
             ev[2].record()
-            y = pkg.ops.causal_conv_silu_varlen(proj[:, :m.conv_dim], m.conv_cache, ids,
-                                                m.conv1d.weight, cu)
-            ev[3].record()
             q, k, v = m._split(y)
             z = proj[:, r[0]:r[1]].view(N, c["HV"], c["DV"])
             core = pkg.ops.chunk_gated_delta_rule_varlen(q, k, v, gg, beta, m.s_cache, ids, cu,
                                                          max(lens), z=z,
                                                          norm_weight=m.norm.weight)
-            ev[4].record()
+            ev[3].record()
             m.out_proj(core.view(N, c["HV"] * c["DV"]))
-            ev[5].record()
+            ev[4].record()
             torch.cuda.synchronize()
-            for i, name in enumerate(["in_proj_gemm", "gate", "conv", "chunk_with_norm",
+            for i, name in enumerate(["in_proj_gemm", "conv_and_gate", "chunk_with_norm",
                                       "out_proj_gemm"]):
                 stages[name] = round(ev[i].elapsed_time(ev[i + 1]), 3)
             del core
@@ -931,11 +929,11 @@ def config4_bench(pkg, dev, world, rank, peaks):
     # the chunk prefill kernels alone on this shard's heads (conv output of the layer's q/k/v)
     with torch.inference_mode():
         proj = torch.nn.functional.linear(x, m._fused_weight())
-        y = pkg.ops.causal_conv_silu_varlen(proj[:, :m.conv_dim], m.conv_cache, ids,
-                                            m.conv1d.weight, cu)
         r = m._proj_rows
-        gg, beta = pkg.ops.fused_g_beta(proj[:, r[1]:r[2]], proj[:, r[2]:r[3]],
-                                        m.A_log[m._v_head_slice], m.dt_bias[m._v_head_slice])
+        y, gg, beta = pkg.ops.conv_gate_varlen(proj[:, :m.conv_dim], m.conv_cache, ids,
+                                               m.conv1d.weight, cu, proj[:, r[1]:r[2]],
+                                               proj[:, r[2]:r[3]], m.A_log[m._v_head_slice],
+                                               m.dt_bias[m._v_head_slice])
         del proj
         q, k, v = m._split(y)
         chunk = lambda: pkg.ops.chunk_gated_delta_rule_varlen(q, k, v, gg, beta, m.s_cache, ids,

@@ -38,7 +38,7 @@
 extern "C" {
 #endif
 
-#define GDN_ABI_VERSION 6
+#define GDN_ABI_VERSION 7
 
 enum gdn_status_code {
   GDN_OK = 0,
@@ -128,6 +128,28 @@ int gdn_causal_conv_silu_varlen(const void* x, int64_t x_row_stride,
                                 int32_t kernel, const void* weight,
                                 void* y, int64_t y_row_stride,
                                 int32_t* status, void* stream);
+
+/*
+ * (a)+(b) The prefill rows' conv and gate in one call: gdn_causal_conv_silu_varlen
+ * and gdn_fused_g_beta (no row mask) on the same rows, the gate computed by an
+ * extra row of CTAs of the conv launch (two launches instead of three; the
+ * results are bit-identical to the two separate calls).  Replaces the
+ * fused_g_beta call and the conv of the varlen prefill (qwen3_5.py:929-946).
+ * Arguments as the two calls: b, a bf16 [n_tokens, num_v_heads] with row stride
+ * ab_row_stride; g fp32 and beta bf16 [n_tokens, num_v_heads] contiguous.
+ */
+int gdn_conv_gate_varlen(const void* x, int64_t x_row_stride,
+                         void* conv_pool, int64_t slot_stride,
+                         int64_t num_slots, const int64_t* ids,
+                         const int32_t* cu_seqlens, int32_t n_seqs,
+                         int64_t n_tokens, int32_t channels,
+                         int32_t kernel, const void* weight,
+                         void* y, int64_t y_row_stride,
+                         const void* b, const void* a, int64_t ab_row_stride,
+                         int32_t num_v_heads, const void* a_log,
+                         const void* dt_bias, int32_t param_dtype,
+                         float* g, void* beta,
+                         int32_t* status, void* stream);
 
 /*
  * (d) One decode step of the gated delta rule, state updated in place in

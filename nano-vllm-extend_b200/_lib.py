@@ -34,6 +34,8 @@ SIGNATURES = {
     "gdn_conv_decode_step": [vp, i64, vp, i64, i64, vp, i32, i32, i32, vp, vp, i64, vp, vp],
     "gdn_causal_conv_silu_varlen": [vp, i64, vp, i64, i64, vp, vp, i32, i64, i32, i32, vp, vp,
                                     i64, vp, vp],
+    "gdn_conv_gate_varlen": [vp, i64, vp, i64, i64, vp, vp, i32, i64, i32, i32, vp, vp, i64,
+                             vp, vp, i64, i32, vp, vp, i32, vp, vp, vp, vp],
     "gdn_recurrent_inplace": [vp, i64, vp, i64, vp, i64, vp, vp, vp, i64, i64, vp, vp, i32, i32,
                               i32, i32, i32, f32, vp, i64, vp, f32, vp, vp],
     "gdn_chunk_prefill_workspace_bytes": [i64, i32, i32, i32, i32],

@@ -121,18 +121,57 @@ __device__ __forceinline__ int find_seq(const int32_t* __restrict__ cu, int n_se
   return lo;
 }
 
+// The g / beta gate of the prefill rows, computed by an extra row of the conv
+// launch (g == nullptr: no gate row).  b / a are the [rows, H] columns of the
+// projection output; g fp32 and beta bf16 are dense [rows, H].
+struct GateArgs {
+  const bf16* b;
+  const bf16* a;
+  int64_t ab_stride;
+  int H;
+  const void* a_log;     // [H] fp32 or bf16 (param_bf16)
+  const void* dt_bias;
+  bool param_bf16;
+  float* g;
+  bf16* beta;
+};
+
+// g / beta of rows [t_begin, t_end): gbeta_kernel's element order and arithmetic
+// (gate_value), so the bits match the separate gate launch.
+__device__ __forceinline__ void gate_rows(const GateArgs& ga, int64_t t_begin, int64_t t_end) {
+  const int64_t n = (t_end - t_begin) * ga.H;
+  for (int64_t i = threadIdx.x; i < n; i += kConvThreads) {
+    const int64_t r = t_begin + i / ga.H;
+    const int h = (int)(i % ga.H);
+    const float al = ga.param_bf16 ? bf2f(static_cast<const bf16*>(ga.a_log)[h])
+                                   : static_cast<const float*>(ga.a_log)[h];
+    const float db = ga.param_bf16 ? bf2f(static_cast<const bf16*>(ga.dt_bias)[h])
+                                   : static_cast<const float*>(ga.dt_bias)[h];
+    float gv, bt;
+    gate_value(bf2f(ga.a[r * ga.ab_stride + h]), bf2f(ga.b[r * ga.ab_stride + h]), al, db, gv,
+               bt);
+    ga.g[r * ga.H + h] = gv;
+    ga.beta[r * ga.H + h] = f2bf(bt);
+  }
+}
+
 template <int K, bool VEC>
 __global__ void __launch_bounds__(kConvThreads) conv_varlen_kernel(
     const bf16* __restrict__ x, int64_t xs, const bf16* __restrict__ pool, int64_t slot_stride,
     int64_t num_slots, const int64_t* __restrict__ ids, const int32_t* __restrict__ cu,
     int n_seqs, int64_t n_tokens, int C, const bf16* __restrict__ w, bf16* __restrict__ y,
-    int64_t ys, int32_t* status) {
+    int64_t ys, int32_t* status, const GateArgs gate) {
   constexpr int T = K - 1;
   constexpr int V = VEC ? 8 : 1;  // channels per thread
-  const int c0 = (blockIdx.y * kConvThreads + threadIdx.x) * V;
   const int64_t t_begin = (int64_t)blockIdx.x * kConvTileTokens;
-  if (c0 >= C || t_begin >= n_tokens) return;
+  if (t_begin >= n_tokens) return;
   const int64_t t_end = min(t_begin + (int64_t)kConvTileTokens, n_tokens);
+  if (gate.g != nullptr && blockIdx.y == gridDim.y - 1) {   // the gate row
+    gate_rows(gate, t_begin, t_end);
+    return;
+  }
+  const int c0 = (blockIdx.y * kConvThreads + threadIdx.x) * V;
+  if (c0 >= C) return;
 
   float wv[V * K];
   if constexpr (VEC) {
@@ -317,6 +356,56 @@ extern "C" int gdn_conv_decode_step(const void* x, int64_t x_row_stride, void* c
   return check_launch("gdn_conv_decode_step");
 }
 
+// The varlen conv (+ the gate row when gate.g is set) and the state roll.
+static int launch_conv_varlen(const char* fn, const void* x, int64_t x_row_stride,
+                              void* conv_pool, int64_t slot_stride, int64_t num_slots,
+                              const int64_t* ids, const int32_t* cu_seqlens, int32_t n_seqs,
+                              int64_t n_tokens, int32_t channels, int32_t kernel,
+                              const void* weight, void* y, int64_t y_row_stride,
+                              const GateArgs& gate, int32_t* status, void* stream) {
+  GDN_REQUIRE(n_seqs >= 0 && n_tokens >= 0 && channels > 0,
+              "%s: bad sizes (n_seqs=%d, n_tokens=%lld, channels=%d)", fn, n_seqs,
+              (long long)n_tokens, channels);
+  GDN_UNSUPPORTED(kernel >= 2 && kernel <= 4, "%s: kernel %d unsupported (2..4)", fn, kernel);
+  GDN_REQUIRE(x_row_stride >= channels && y_row_stride >= channels,
+              "%s: row stride smaller than channels", fn);
+  GDN_REQUIRE(num_slots > 0 && slot_stride >= (int64_t)channels * (kernel - 1),
+              "%s: slot_stride too small", fn);
+  GDN_REQUIRE(n_seqs > 0 || n_tokens == 0, "%s: tokens without sequences", fn);
+  if (n_seqs == 0) return GDN_OK;
+  GDN_REQUIRE(x && conv_pool && ids && cu_seqlens && weight && y, "%s: null pointer", fn);
+  const bool vec = channels % 8 == 0 && x_row_stride % 8 == 0 && y_row_stride % 8 == 0 &&
+                   aligned16(x) && aligned16(y) && aligned16(weight);
+  cudaStream_t s = (cudaStream_t)stream;
+  const int per_cta = vec ? kConvThreads * 8 : kConvThreads;
+  const int64_t tiles = (n_tokens + kConvTileTokens - 1) / kConvTileTokens;
+  GDN_UNSUPPORTED(tiles < (1ll << 31), "%s: too many tokens", fn);
+  const unsigned conv_rows = (unsigned)((channels + per_cta - 1) / per_cta);
+  dim3 wgrid((channels + kConvThreads - 1) / kConvThreads, n_seqs);
+#define GDN_VL(KK)                                                                               \
+  if (kernel == KK) {                                                                            \
+    if (tiles > 0) {                                                                             \
+      dim3 grid((unsigned)tiles, conv_rows + (gate.g != nullptr ? 1u : 0u));                     \
+      if (vec)                                                                                   \
+        conv_varlen_kernel<KK, true><<<grid, kConvThreads, 0, s>>>(                              \
+            (const bf16*)x, x_row_stride, (const bf16*)conv_pool, slot_stride, num_slots, ids,   \
+            cu_seqlens, n_seqs, n_tokens, channels, (const bf16*)weight, (bf16*)y, y_row_stride, \
+            status, gate);                                                                       \
+      else                                                                                       \
+        conv_varlen_kernel<KK, false><<<grid, kConvThreads, 0, s>>>(                             \
+            (const bf16*)x, x_row_stride, (const bf16*)conv_pool, slot_stride, num_slots, ids,   \
+            cu_seqlens, n_seqs, n_tokens, channels, (const bf16*)weight, (bf16*)y, y_row_stride, \
+            status, gate);                                                                       \
+    }                                                                                            \
+    conv_state_writeback_kernel<KK><<<wgrid, kConvThreads, 0, s>>>(                              \
+        (const bf16*)x, x_row_stride, (bf16*)conv_pool, slot_stride, num_slots, ids, cu_seqlens, \
+        channels, n_tokens, status);                                                             \
+  }
+  GDN_VL(2) GDN_VL(3) GDN_VL(4)
+#undef GDN_VL
+  return check_launch(fn);
+}
+
 extern "C" int gdn_causal_conv_silu_varlen(const void* x, int64_t x_row_stride, void* conv_pool,
                                            int64_t slot_stride, int64_t num_slots,
                                            const int64_t* ids, const int32_t* cu_seqlens,
@@ -324,46 +413,31 @@ extern "C" int gdn_causal_conv_silu_varlen(const void* x, int64_t x_row_stride, 
                                            int32_t kernel, const void* weight, void* y,
                                            int64_t y_row_stride, int32_t* status, void* stream) {
   clear_error();
-  GDN_REQUIRE(n_seqs >= 0 && n_tokens >= 0 && channels > 0,
-              "gdn_causal_conv_silu_varlen: bad sizes (n_seqs=%d, n_tokens=%lld, channels=%d)",
-              n_seqs, (long long)n_tokens, channels);
-  GDN_UNSUPPORTED(kernel >= 2 && kernel <= 4,
-                  "gdn_causal_conv_silu_varlen: kernel %d unsupported (2..4)", kernel);
-  GDN_REQUIRE(x_row_stride >= channels && y_row_stride >= channels,
-              "gdn_causal_conv_silu_varlen: row stride smaller than channels");
-  GDN_REQUIRE(num_slots > 0 && slot_stride >= (int64_t)channels * (kernel - 1),
-              "gdn_causal_conv_silu_varlen: slot_stride too small");
-  GDN_REQUIRE(n_seqs > 0 || n_tokens == 0, "gdn_causal_conv_silu_varlen: tokens without sequences");
-  if (n_seqs == 0) return GDN_OK;
-  GDN_REQUIRE(x && conv_pool && ids && cu_seqlens && weight && y,
-              "gdn_causal_conv_silu_varlen: null pointer");
-  const bool vec = channels % 8 == 0 && x_row_stride % 8 == 0 && y_row_stride % 8 == 0 &&
-                   aligned16(x) && aligned16(y) && aligned16(weight);
-  cudaStream_t s = (cudaStream_t)stream;
-  const int per_cta = vec ? kConvThreads * 8 : kConvThreads;
-  const int64_t tiles = (n_tokens + kConvTileTokens - 1) / kConvTileTokens;
-  GDN_UNSUPPORTED(tiles < (1ll << 31), "gdn_causal_conv_silu_varlen: too many tokens");
-  dim3 wgrid((channels + kConvThreads - 1) / kConvThreads, n_seqs);
-#define GDN_VL(KK)                                                                               \
-  if (kernel == KK) {                                                                            \
-    if (tiles > 0) {                                                                             \
-      dim3 grid((unsigned)tiles, (channels + per_cta - 1) / per_cta);                            \
-      if (vec)                                                                                   \
-        conv_varlen_kernel<KK, true><<<grid, kConvThreads, 0, s>>>(                              \
-            (const bf16*)x, x_row_stride, (const bf16*)conv_pool, slot_stride, num_slots, ids,   \
-            cu_seqlens, n_seqs, n_tokens, channels, (const bf16*)weight, (bf16*)y, y_row_stride, \
-            status);                                                                             \
-      else                                                                                       \
-        conv_varlen_kernel<KK, false><<<grid, kConvThreads, 0, s>>>(                             \
-            (const bf16*)x, x_row_stride, (const bf16*)conv_pool, slot_stride, num_slots, ids,   \
-            cu_seqlens, n_seqs, n_tokens, channels, (const bf16*)weight, (bf16*)y, y_row_stride, \
-            status);                                                                             \
-    }                                                                                            \
-    conv_state_writeback_kernel<KK><<<wgrid, kConvThreads, 0, s>>>(                              \
-        (const bf16*)x, x_row_stride, (bf16*)conv_pool, slot_stride, num_slots, ids, cu_seqlens, \
-        channels, n_tokens, status);                                                                    \
-  }
-  GDN_VL(2) GDN_VL(3) GDN_VL(4)
-#undef GDN_VL
-  return check_launch("gdn_causal_conv_silu_varlen");
+  const GateArgs none{};
+  return launch_conv_varlen("gdn_causal_conv_silu_varlen", x, x_row_stride, conv_pool,
+                            slot_stride, num_slots, ids, cu_seqlens, n_seqs, n_tokens, channels,
+                            kernel, weight, y, y_row_stride, none, status, stream);
+}
+
+extern "C" int gdn_conv_gate_varlen(const void* x, int64_t x_row_stride, void* conv_pool,
+                                    int64_t slot_stride, int64_t num_slots, const int64_t* ids,
+                                    const int32_t* cu_seqlens, int32_t n_seqs, int64_t n_tokens,
+                                    int32_t channels, int32_t kernel, const void* weight, void* y,
+                                    int64_t y_row_stride, const void* b, const void* a,
+                                    int64_t ab_row_stride, int32_t num_v_heads,
+                                    const void* a_log, const void* dt_bias, int32_t param_dtype,
+                                    float* g, void* beta, int32_t* status, void* stream) {
+  clear_error();
+  const char* fn = "gdn_conv_gate_varlen";
+  GDN_REQUIRE(num_v_heads > 0, "%s: bad sizes (heads=%d)", fn, num_v_heads);
+  GDN_REQUIRE(ab_row_stride >= num_v_heads, "%s: row stride %lld < heads %d", fn,
+              (long long)ab_row_stride, num_v_heads);
+  GDN_REQUIRE(param_dtype == GDN_DTYPE_F32 || param_dtype == GDN_DTYPE_BF16,
+              "%s: param_dtype must be F32 or BF16", fn);
+  GDN_REQUIRE(n_tokens == 0 || (b && a && a_log && dt_bias && g && beta), "%s: null pointer", fn);
+  GateArgs gate{(const bf16*)b, (const bf16*)a, ab_row_stride, num_v_heads, a_log, dt_bias,
+                param_dtype == GDN_DTYPE_BF16, g, (bf16*)beta};
+  return launch_conv_varlen(fn, x, x_row_stride, conv_pool, slot_stride, num_slots, ids,
+                            cu_seqlens, n_seqs, n_tokens, channels, kernel, weight, y,
+                            y_row_stride, gate, status, stream);
 }

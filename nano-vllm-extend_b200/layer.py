@@ -69,7 +69,7 @@ class Qwen3_5GatedDeltaNet(nn.Module):
     # step).  See ops.poll_status for graph-replayed steps.
     report_status = True
     # Mark the layer's phases with NVTX ranges ("gdn.in_proj", "gdn.decode_core",
-    # "gdn.gate", "gdn.conv", "gdn.chunk", "gdn.out_proj") for nsys-style
+    # "gdn.conv_gate", "gdn.chunk", "gdn.out_proj") for nsys-style
     # timelines; off by default (a range costs a host call per phase).
     nvtx = False
 
@@ -201,11 +201,8 @@ class Qwen3_5GatedDeltaNet(nn.Module):
         if n1 < N:
             cu_q = ctx.cu_seqlens_q
             cu_p = cu_q[n1:] - cu_q[n1] if n1 else cu_q
-            with self._range("gdn.gate"):
-                g, beta = ops.fused_g_beta(b[n1:], a[n1:], self.A_log[self._v_head_slice],
-                                           self.dt_bias[self._v_head_slice], None)
-            self._prefill_core(mixed[n1:], g, beta, ids[n1:], cu_p, max(lens_q[n1:]), z[n1:],
-                               out=core[n1:])
+            self._prefill_core(mixed[n1:], b[n1:], a[n1:], ids[n1:], cu_p, max(lens_q[n1:]),
+                               z[n1:], out=core[n1:])
         if self.report_status and ops.is_status_publisher(self, hidden_states.device):
             ops.publish_status(hidden_states.device)
         with self._range("gdn.out_proj"):
@@ -241,13 +238,15 @@ class Qwen3_5GatedDeltaNet(nn.Module):
             return out
         return o
 
-    def _prefill_core(self, mixed, g, beta, ids, cu_seqlens, max_seqlen, z, out=None):
-        """Prefill rows: varlen conv + chunked rule with slot states + gated
-        norm (the composition of qwen3_5.py:922-963, unpadded)."""
-        with self._range("gdn.conv"):
-            y = ops.causal_conv_silu_varlen(
+    def _prefill_core(self, mixed, b, a, ids, cu_seqlens, max_seqlen, z, out=None):
+        """Prefill rows: varlen conv and g / beta gate (one call) + chunked rule
+        with slot states + gated norm (the composition of qwen3_5.py:922-963,
+        unpadded)."""
+        with self._range("gdn.conv_gate"):
+            y, g, beta = ops.conv_gate_varlen(
                 mixed, self.conv_cache, ids,
-                self.conv1d.weight.view(self.conv_dim, self.conv_kernel), cu_seqlens)
+                self.conv1d.weight.view(self.conv_dim, self.conv_kernel), cu_seqlens, b, a,
+                self.A_log[self._v_head_slice], self.dt_bias[self._v_head_slice])
         q, k, v = self._split(y)
         with self._range("gdn.chunk"):
             return ops.chunk_gated_delta_rule_varlen(

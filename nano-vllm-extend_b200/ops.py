@@ -299,6 +299,49 @@ def causal_conv_silu_varlen(x: torch.Tensor, state_pool: torch.Tensor, ids: torc
     return y
 
 
+def conv_gate_varlen(x: torch.Tensor, state_pool: torch.Tensor, ids: torch.Tensor,
+                     weight: torch.Tensor, cu_seqlens: torch.Tensor, b: torch.Tensor,
+                     a: torch.Tensor, a_log: torch.Tensor, dt_bias: torch.Tensor):
+    """:func:`causal_conv_silu_varlen` and :func:`fused_g_beta` (no mask) of
+    the same prefill rows in one call (qwen3_5.py:929-946): the gate runs as an
+    extra row of the conv launch.  Bit-identical to the two calls.
+    Returns (y [N, C], g fp32 [N, Vh], beta bf16 [N, Vh])."""
+    _cuda(x, state_pool, ids, weight, cu_seqlens, b, a, a_log, dt_bias)
+    C = x.shape[-1]
+    w = weight.reshape(C, -1).contiguous()
+    K = w.shape[1]
+    _pool_view_check(state_pool, K - 1, C)
+    x2, xs = _rows2d(x, C)
+    N = x2.shape[0]
+    ids = _ids64(ids)
+    cu = cu_seqlens.to(torch.int32).contiguous() if cu_seqlens.dtype != torch.int32 \
+        else cu_seqlens.contiguous()
+    assert cu.numel() == ids.numel() + 1, "cu_seqlens must have n_seqs + 1 entries"
+    assert b.dtype == torch.bfloat16 and a.dtype == torch.bfloat16 and a.shape == b.shape
+    vh = a.shape[-1]
+    assert a.reshape(-1, vh).shape[0] == N, "b / a need one row per token"
+    assert a_log.numel() == vh and dt_bias.numel() == vh and a_log.dtype == dt_bias.dtype
+    if a.dim() != 2 or b.dim() != 2 or a.stride(0) != b.stride(0) or a.stride(1) != 1 \
+            or b.stride(1) != 1:
+        a = a.reshape(-1, vh).contiguous()
+        b = b.reshape(-1, vh).contiguous()
+    pdt = _lib.GDN_DTYPE_BF16 if a_log.dtype == torch.bfloat16 else _lib.GDN_DTYPE_F32
+    if pdt == _lib.GDN_DTYPE_F32:
+        a_log, dt_bias = a_log.float().contiguous(), dt_bias.float().contiguous()
+    else:
+        a_log, dt_bias = a_log.contiguous(), dt_bias.contiguous()
+    y = torch.empty(N, C, dtype=x.dtype, device=x.device)
+    g = torch.empty(N, vh, dtype=torch.float32, device=x.device)
+    beta = torch.empty(N, vh, dtype=torch.bfloat16, device=x.device)
+    rc = _lib.load().gdn_conv_gate_varlen(
+        _p(x2), xs, _p(state_pool), _slot_stride(state_pool), state_pool.shape[0], _p(ids), _p(cu),
+        ids.numel(), N, C, K, _p(w), _p(y), y.stride(0), _p(b), _p(a), a.stride(0), vh,
+        _p(a_log), _p(dt_bias), pdt, _p(g), _p(beta), _p(status_word(x.device)),
+        _stream_ptr(x.device))
+    _lib.check(rc, "gdn_conv_gate_varlen")
+    return y, g, beta
+
+
 # ---------------------------------------------------------------------------
 # (d) recurrent decode, (c) chunk prefill
 # ---------------------------------------------------------------------------

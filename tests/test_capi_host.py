@@ -20,7 +20,7 @@ def declared_symbols():
 def test_header_declares_the_path():
     syms = declared_symbols()
     for s in ("gdn_fused_g_beta", "gdn_conv_decode_step", "gdn_causal_conv_silu_varlen",
-              "gdn_recurrent_inplace", "gdn_chunk_prefill_varlen", "gdn_rms_norm_gated",
+              "gdn_conv_gate_varlen", "gdn_recurrent_inplace", "gdn_chunk_prefill_varlen", "gdn_rms_norm_gated",
               "gdn_decode_fused", "gdn_abi_version", "gdn_last_error"):
         assert s in syms
 
@@ -68,6 +68,22 @@ def test_host_validation_errors(pkg):
     rc, msg = _call(pkg, "gdn_causal_conv_silu_varlen", None, 64, None, 1000, 2, None, None, 0,
                     10, 64, 4, None, None, 64, None, None)
     assert rc == L.GDN_ERR_INVALID_ARGUMENT
+    # conv + gate: the gate's checks, then the conv's (named after the combined call)
+    fake = 1 << 20                                   # aligned, never dereferenced
+    conv = (fake, 64, fake, 1000, 2, fake, fake, 1, 10, 64, 4, fake, fake, 64)
+    rc, msg = _call(pkg, "gdn_conv_gate_varlen", *conv, fake, fake, 8, 8, fake, fake, 7, fake,
+                    fake, None, None)
+    assert rc == L.GDN_ERR_INVALID_ARGUMENT and "param_dtype" in msg
+    rc, msg = _call(pkg, "gdn_conv_gate_varlen", *conv, fake, fake, 4, 8, fake, fake, 0, fake,
+                    fake, None, None)
+    assert rc == L.GDN_ERR_INVALID_ARGUMENT and "row stride" in msg
+    rc, msg = _call(pkg, "gdn_conv_gate_varlen", *conv, None, fake, 8, 8, fake, fake, 0, fake,
+                    fake, None, None)
+    assert rc == L.GDN_ERR_INVALID_ARGUMENT and "null pointer" in msg
+    rc, msg = _call(pkg, "gdn_conv_gate_varlen", fake, 64, fake, 1000, 2, fake, fake, 0, 10, 64,
+                    4, fake, fake, 64, fake, fake, 8, 8, fake, fake, 0, fake, fake, None, None)
+    assert rc == L.GDN_ERR_INVALID_ARGUMENT
+    assert msg.startswith("gdn_conv_gate_varlen:") and "without sequences" in msg
     # gate: bad param dtype
     rc, msg = _call(pkg, "gdn_fused_g_beta", None, None, 8, 4, 8, None, None, 7, None, None,
                     None, None)

@@ -144,6 +144,32 @@ def test_conv_varlen_vs_oracle(ops, C):
     ops.check_status()
 
 
+@pytest.mark.parametrize("C,pdt", [(1024, torch.bfloat16), (100, torch.float32)])
+def test_conv_gate_varlen_equals_separate_calls(ops, C, pdt):
+    """The combined conv + gate call gives the bits of causal_conv_silu_varlen
+    and fused_g_beta run separately: y, g, beta and the rolled states, on
+    ragged sequences (empty ones included), b / a as strided column views of
+    one projection row (the layer's layout), vector and scalar conv paths."""
+    r = I.rng(33)
+    lens = [0, 1, 2, 3, 31, 32, 33, 100, 0, 5, 700]
+    N, K, slots, HV = sum(lens), 4, 14, 16
+    proj = bf(r.standard_normal((N, C + 2 * HV + 8)).astype(np.float32))
+    x, b, a = proj[:, :C], proj[:, C:C + HV], proj[:, C + HV:C + 2 * HV]
+    w = bf(r.uniform(-0.6, 0.6, (C, K)).astype(np.float32))
+    a_log = torch.from_numpy(r.uniform(-1, 0, HV).astype(np.float32)).to(DEV).to(pdt)
+    dt_bias = torch.from_numpy(r.standard_normal(HV).astype(np.float32)).to(DEV).to(pdt)
+    pool = bf(r.standard_normal((slots, C, K - 1)).astype(np.float32))
+    ids = i64(r.permutation(slots)[:len(lens)])
+    cu = i32(I.cu_from_lens(lens))
+    p1, p2 = pool.clone(), pool.clone()
+    y1 = ops.causal_conv_silu_varlen(x, p1, ids, w, cu)
+    g1, b1 = ops.fused_g_beta(b, a, a_log, dt_bias)
+    y2, g2, b2 = ops.conv_gate_varlen(x, p2, ids, w, cu, b, a, a_log, dt_bias)
+    ops.check_status()
+    for u, v in ((y1, y2), (g1, g2), (b1, b2), (p1, p2)):
+        assert u.shape == v.shape and torch.equal(u, v)
+
+
 def test_conv_padded_golden_rows(ops, golden_dir):
     """Rows of the reference's padded conv whose writeback is at T match the
     varlen kernel (values and state)."""
