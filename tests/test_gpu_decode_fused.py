@@ -107,6 +107,7 @@ CASES = [
     (16, 32, 128, 4, 300, torch.float32),   # 4800 groups: many per CTA, the stage ring wraps
     (1, 4, 64, 4, 5, torch.bfloat16),
     (4, 4, 64, 3, 33, torch.float32),       # one v-head per k-head
+    (4, 4, 64, 3, 1200, torch.bfloat16),    # one unit per group, 8 groups per CTA
     (2, 8, 128, 2, 3, torch.bfloat16),      # four v-heads per k-head
 ]
 
