@@ -628,9 +628,9 @@ def prefill_bench(pkg, device, steps, peaks):
     # gated norm alone.  Every measured call runs once untimed first, so the
     # caching allocator already holds its output blocks (a fresh multi-GB
     # cudaMalloc next to the 40 GB decode stack costs ~100 ms).
-    stages = {}
+    stage_runs = {}
     with torch.inference_mode():
-        for rep in range(2):
+        for rep in range(4):   # one untimed pass, then the median of three
             ev = [torch.cuda.Event(enable_timing=True) for _ in range(8)]
             pools.reset(ids)
             ev[0].record()
@@ -652,11 +652,13 @@ def prefill_bench(pkg, device, steps, peaks):
             torch.cuda.synchronize()
             for i, name in enumerate(["in_proj_gemm", "conv_and_gate", "chunk_with_norm",
                                       "out_proj_gemm"]):
-                stages[name] = round(ev[i].elapsed_time(ev[i + 1]), 3)
+                if rep > 0:
+                    stage_runs.setdefault(name, []).append(ev[i].elapsed_time(ev[i + 1]))
             del core
-            if rep == 0:   # free the first pass's buffers before the timed pass allocates
+            if rep < 3:    # free this pass's buffers before the next pass allocates
                 del proj, gg, beta, y, q, k, v, z
                 torch.cuda.synchronize()
+        stages = {k: round(statistics.median(v), 3) for k, v in stage_runs.items()}
         pkg.ops.chunk_gated_delta_rule_varlen(q, k, v, gg, beta, m.s_cache, ids, cu, max(lens))
         torch.cuda.synchronize()
         clocks = Clocks(device.index if device.index is not None else 0)
@@ -1306,10 +1308,13 @@ def profile_case(pkg, name):
         cu = torch.tensor(np.concatenate([[0], np.cumsum(lens)]), dtype=torch.int32, device=dev)
         ids = torch.arange(len(lens), device=dev)
         x = torch.randn(N, C, generator=g, device=dev).to(torch.bfloat16)
-        if name == "conv_varlen":
+        if name == "conv_varlen":      # the layer's call: conv + the gate row, b / a columns
+            xb = torch.randn(N, C + 2 * HV, generator=g, device=dev).to(torch.bfloat16)
             pool = torch.randn(len(lens), C, 3, generator=g, device=dev).to(torch.bfloat16)
             w = torch.randn(C, 4, generator=g, device=dev).to(torch.bfloat16)
-            fn = lambda: ops.causal_conv_silu_varlen(x, pool, ids, w, cu)
+            al = torch.rand(HV, device=dev)
+            fn = lambda: ops.conv_gate_varlen(xb[:, :C], pool, ids, w, cu, xb[:, C:C + HV],
+                                              xb[:, C + HV:], al, al)
         elif name == "chunk":
             pool = torch.zeros(len(lens), HV, D, D, device=dev)
             q = x[:, :HK * D].view(N, HK, D)
