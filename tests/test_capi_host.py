@@ -131,6 +131,10 @@ def test_empty_calls_are_noops(pkg):
     assert rc == L.GDN_ERR_INVALID_ARGUMENT and "norm" in msg
     assert _call(pkg, "gdn_fused_g_beta", None, None, 8, 0, 8, None, None, 0, None, None, None,
                  None)[0] == L.GDN_OK
+    # conv + gate with no sequences and no tokens: nothing to launch
+    assert _call(pkg, "gdn_conv_gate_varlen", None, 64, None, 1000, 2, None, None, 0, 0, 64, 4,
+                 None, None, 64, None, None, 8, 8, None, None, 0, None, None, None,
+                 None)[0] == L.GDN_OK
 
 
 def test_python_errors_map_from_codes(pkg):
