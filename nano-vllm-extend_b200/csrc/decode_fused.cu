@@ -36,6 +36,7 @@
 // GDN_STATUS_TIMEOUT, drains the copies it has in flight (bounded again) and
 // returns.
 #include <algorithm>
+#include <atomic>
 
 #include <mutex>
 
@@ -718,10 +719,10 @@ static int launch_decode_head(int64_t units, cudaStream_t s, const bf16* mixed, 
   const size_t smem = sizeof(HeadSmem<D>) + 128;   // + alignment slack
   static_assert(HeadCfg<D>::CTAS * (sizeof(HeadSmem<D>) + 128 + 1024) <= 228 * 1024,
                 "the CTAs per SM must fit the shared memory");
-  static int configured[64] = {0};
+  static std::atomic<int> configured[64];   // concurrent first calls set the same limit
   int dev = 0;
   cudaGetDevice(&dev);
-  if (dev >= 0 && dev < 64 && !configured[dev]) {
+  if (dev < 0 || dev >= 64 || !configured[dev].load(std::memory_order_relaxed)) {
     const cudaError_t e = cudaFuncSetAttribute(
         decode_head_kernel<D, K>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) {
@@ -729,7 +730,7 @@ static int launch_decode_head(int64_t units, cudaStream_t s, const bf16* mixed, 
                 cudaGetErrorString(e));
       return GDN_ERR_CUDA;
     }
-    configured[dev] = 1;
+    if (dev >= 0 && dev < 64) configured[dev].store(1, std::memory_order_relaxed);
   }
   decode_head_kernel<D, K><<<(unsigned)units, HeadCfg<D>::NT, smem, s>>>(
       mixed, ms, z, zs, b, a, abs_, conv_pool, conv_ss, conv_w, a_log, dt_bias, param_f32, pool,
@@ -750,10 +751,10 @@ static int launch_decode_fused(int grid, cudaStream_t s, const CUtensorMap& tm,
   const size_t smem = sizeof(DecSmem<D>) + 128;   // + alignment slack
   static_assert(DecCfg<D>::CTAS * (sizeof(DecSmem<D>) + 128 + 1024) <= 228 * 1024,
                 "the CTAs per SM must fit the shared memory");
-  static int configured[64] = {0};
+  static std::atomic<int> configured[64];   // concurrent first calls set the same limit
   int dev = 0;
   cudaGetDevice(&dev);
-  if (dev >= 0 && dev < 64 && !configured[dev]) {
+  if (dev < 0 || dev >= 64 || !configured[dev].load(std::memory_order_relaxed)) {
     const cudaError_t e = cudaFuncSetAttribute(
         decode_fused_kernel<D, K>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) {
@@ -761,7 +762,7 @@ static int launch_decode_fused(int grid, cudaStream_t s, const CUtensorMap& tm,
                 cudaGetErrorString(e));
       return GDN_ERR_CUDA;
     }
-    configured[dev] = 1;
+    if (dev >= 0 && dev < 64) configured[dev].store(1, std::memory_order_relaxed);
   }
   decode_fused_kernel<D, K><<<grid, DecCfg<D>::NT, smem, s>>>(
       tm, mixed, ms, z, zs, b, a, abs_, conv_pool, conv_ss, conv_w, a_log, dt_bias, param_f32,
