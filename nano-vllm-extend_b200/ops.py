@@ -23,11 +23,16 @@ in a per-device status word.  Two ways read it:
   one whose kernels saw it and raises at the next poll after that; an engine
   that replays whole decode steps from a CUDA graph calls
   :func:`poll_status` between steps.
+
+Optional host-side checks (:func:`set_debug_checks`, or ``GDN_DEBUG_CHECKS=1``)
+validate slot ids and ``cu_seqlens`` before each launch and raise at once.
 """
 from __future__ import annotations
 
+import os
 import weakref
 
+import numpy as np
 import torch
 
 from . import _lib
@@ -151,6 +156,58 @@ def set_wait_limit(polls: int | None) -> None:
     _lib.load().gdn_set_wait_limit(-1 if polls is None else int(polls))
 
 
+_DEBUG_CHECKS = os.environ.get("GDN_DEBUG_CHECKS", "0") not in ("", "0")
+
+
+def set_debug_checks(on: bool) -> None:
+    """Host-side argument checks before every launch (off by default; also
+    on with ``GDN_DEBUG_CHECKS=1``): slot ids inside the pool and not repeated
+    within one call, except the pool's last slot (the engine's dummy slot,
+    which CUDA-graph pad rows share); ``cu_seqlens`` starting at 0,
+    non-decreasing and ending at the row count.  Each check copies the ids /
+    ``cu_seqlens`` to the host, a synchronisation, so checks are skipped while
+    a CUDA graph is being captured.  The kernels' own handling stays as it is:
+    without the checks a bad slot is skipped and flagged in the status word,
+    and repeated slots are undefined, as in the reference."""
+    global _DEBUG_CHECKS
+    _DEBUG_CHECKS = bool(on)
+
+
+def check_slot_ids(ids, num_slots: int) -> None:
+    """Raise IndexError for a slot id outside [0, num_slots) and ValueError
+    for a slot id given more than once (the last slot excepted)."""
+    v = np.asarray(ids.cpu() if isinstance(ids, torch.Tensor) else ids, np.int64).reshape(-1)
+    bad = (v < 0) | (v >= num_slots)
+    if bad.any():
+        raise IndexError(f"slot id {int(v[bad][0])} outside the pool of {num_slots} slots")
+    u, n = np.unique(v[v != num_slots - 1], return_counts=True)
+    if (n > 1).any():
+        raise ValueError(f"slot id {int(u[n > 1][0])} appears {int(n[n > 1][0])} times in "
+                         "one call (the rows would race on its state)")
+
+
+def check_cu_seqlens(cu, n_rows: int, max_seqlen: int | None = None) -> None:
+    """Raise ValueError unless cu starts at 0, never decreases and ends at
+    n_rows, and (when given) no sequence is longer than max_seqlen."""
+    c = np.asarray(cu.cpu() if isinstance(cu, torch.Tensor) else cu, np.int64).reshape(-1)
+    if c.size == 0 or c[0] != 0 or c[-1] != n_rows or (np.diff(c) < 0).any():
+        raise ValueError(f"cu_seqlens must start at 0, not decrease and end at {n_rows} "
+                         f"(got {c[:4].tolist()} ... {c[-2:].tolist()})")
+    if max_seqlen is not None and c.size > 1 and int(np.diff(c).max()) > max_seqlen:
+        raise ValueError(f"a sequence of {int(np.diff(c).max())} rows exceeds max_seqlen "
+                         f"{max_seqlen}")
+
+
+def _debug_checks(ids=None, num_slots: int = 0, cu=None, n_rows: int = 0,
+                  max_seqlen: int | None = None) -> None:
+    if not _DEBUG_CHECKS or torch.cuda.is_current_stream_capturing():
+        return
+    if ids is not None:
+        check_slot_ids(ids, num_slots)
+    if cu is not None:
+        check_cu_seqlens(cu, n_rows, max_seqlen)
+
+
 def _out_buffer(out, shape, device) -> torch.Tensor:
     """A bf16 output of `shape`: `out` itself when given (a contiguous tensor of
     that shape, e.g. a row slice of a larger buffer), else a new tensor."""
@@ -264,6 +321,7 @@ def conv_decode_step(x: torch.Tensor, state_pool: torch.Tensor, ids: torch.Tenso
     n = x2.shape[0]
     ids = _ids64(ids)
     assert ids.numel() == n
+    _debug_checks(ids, state_pool.shape[0])
     y = torch.empty(n, C, dtype=x.dtype, device=x.device)
     rc = _lib.load().gdn_conv_decode_step(
         _p(x2), xs, _p(state_pool), _slot_stride(state_pool), state_pool.shape[0], _p(ids), n, C, K,
@@ -290,6 +348,7 @@ def causal_conv_silu_varlen(x: torch.Tensor, state_pool: torch.Tensor, ids: torc
     cu = cu_seqlens.to(torch.int32).contiguous() if cu_seqlens.dtype != torch.int32 \
         else cu_seqlens.contiguous()
     assert cu.numel() == ids.numel() + 1, "cu_seqlens must have n_seqs + 1 entries"
+    _debug_checks(ids, state_pool.shape[0], cu, N)
     y = torch.empty(N, C, dtype=x.dtype, device=x.device)
     rc = _lib.load().gdn_causal_conv_silu_varlen(
         _p(x2), xs, _p(state_pool), _slot_stride(state_pool), state_pool.shape[0], _p(ids), _p(cu),
@@ -317,6 +376,7 @@ def conv_gate_varlen(x: torch.Tensor, state_pool: torch.Tensor, ids: torch.Tenso
     cu = cu_seqlens.to(torch.int32).contiguous() if cu_seqlens.dtype != torch.int32 \
         else cu_seqlens.contiguous()
     assert cu.numel() == ids.numel() + 1, "cu_seqlens must have n_seqs + 1 entries"
+    _debug_checks(ids, state_pool.shape[0], cu, N)
     assert b.dtype == torch.bfloat16 and a.dtype == torch.bfloat16 and a.shape == b.shape
     vh = a.shape[-1]
     assert a.reshape(-1, vh).shape[0] == N, "b / a need one row per token"
@@ -402,6 +462,7 @@ def recurrent_gdn_inplace(q, k, v, g, beta, s_pool, ids, z=None, norm_weight=Non
     _state_view_check(s_pool, HV, DK, DV)
     ids = _ids64(ids)
     assert ids.numel() == bs
+    _debug_checks(ids, s_pool.shape[0])
     z3, zs, nw = _norm_args(z, norm_weight, bs, HV, DV)
     out = torch.empty(bs, 1, HV, DV, dtype=v.dtype, device=v.device)
     rc = _lib.load().gdn_recurrent_inplace(
@@ -464,6 +525,7 @@ def chunk_gated_delta_rule_varlen(q, k, v, g, beta, s_pool, ids, cu_seqlens,
     cu = cu_seqlens.to(torch.int32).contiguous() if cu_seqlens.dtype != torch.int32 \
         else cu_seqlens.contiguous()
     assert cu.numel() == ids.numel() + 1
+    _debug_checks(ids, s_pool.shape[0], cu, N, int(max_seqlen))
     z3, zs, nw = _norm_args(z, norm_weight, N, HV, DV)
     out = _out_buffer(out, (N, HV, DV), v.device)
     ws_bytes = chunk_prefill_workspace_bytes(N, ids.numel(), HV, DK, DV) if split else 0
@@ -586,6 +648,7 @@ def decode_fused(mixed: torch.Tensor, z: torch.Tensor, b: torch.Tensor, a: torch
     ids = _ids64(ids)
     assert ids.numel() == bs
     assert conv_pool.shape[0] == s_pool.shape[0], "both pools index the same slots"
+    _debug_checks(ids, s_pool.shape[0])
     out = _out_buffer(out, (bs, HV, D), mixed.device)
     cnt = group_counters(mixed.device, bs * HK) if counters else None
     rc = _lib.load().gdn_decode_fused(

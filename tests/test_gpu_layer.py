@@ -252,3 +252,27 @@ def test_layer_nvtx_ranges_leave_results_unchanged(L):
         outs.append((y0, y1, m.s_cache.clone()))
     for a, b in zip(*outs):
         assert torch.equal(a, b)
+
+
+def test_debug_checks_raise_before_any_launch(L):
+    """With the host-side checks on, a slot id outside the pool raises
+    IndexError and a repeated one ValueError in the call itself, before any
+    GDN kernel launches, so the device status word stays clear; repeats of the
+    pool's last slot (the dummy slot of graph pad rows) pass."""
+    c = I.C0
+    W = I.layer_weights(c["hidden"], c["HK"], c["DK"], c["HV"], c["DV"], c["K"], seed=15)
+    m = build_layer(L, cfg_c0(), W)
+    m.s_cache = torch.zeros(4, c["HV"], c["DK"], c["DV"], device=DEV)
+    m.conv_cache = torch.zeros(4, m.conv_dim, c["K"] - 1, dtype=torch.bfloat16, device=DEV)
+    L.ops.check_status()
+    L.ops.set_debug_checks(True)
+    try:
+        with pytest.raises(IndexError):
+            run(L, m, I.layer_hidden(2, c["hidden"], seed=1), [0, 9], [1, 1])
+        with pytest.raises(ValueError):
+            run(L, m, I.layer_hidden(5, c["hidden"], seed=2), [1, 1], [2, 3])   # prefill rows
+        run(L, m, I.layer_hidden(3, c["hidden"], seed=3), [0, 3, 3], [1, 1, 1])   # dummy slot 3
+        torch.cuda.synchronize()
+        assert L.ops.check_status() == 0
+    finally:
+        L.ops.set_debug_checks(False)

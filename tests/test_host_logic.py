@@ -139,3 +139,29 @@ def test_ops_reject_cpu_tensors(pkg):
         ops.rms_norm_gated(torch.zeros(2, 64, dtype=torch.bfloat16),
                            torch.zeros(2, 64, dtype=torch.bfloat16),
                            torch.ones(64, dtype=torch.bfloat16), 1e-6)
+
+
+def test_debug_checks_of_slot_ids_and_cu_seqlens(pkg):
+    """The optional host-side checks: ids inside the pool and unrepeated
+    (the last slot, the engine's dummy slot for graph pad rows, may repeat);
+    cu_seqlens from 0, non-decreasing, ending at the row count, no sequence
+    longer than max_seqlen.  Off by default."""
+    ops = pkg.ops
+    assert ops._DEBUG_CHECKS is False
+    ops.check_slot_ids(torch.tensor([3, 0, 7, 7, 7]), 8)     # 7 is the dummy slot
+    with pytest.raises(IndexError):
+        ops.check_slot_ids(torch.tensor([0, 8]), 8)
+    with pytest.raises(IndexError):
+        ops.check_slot_ids([-1], 8)
+    with pytest.raises(ValueError, match="appears 2 times"):
+        ops.check_slot_ids(torch.tensor([2, 5, 2]), 8)
+    ops.check_cu_seqlens(torch.tensor([0, 3, 3, 10], dtype=torch.int32), 10, max_seqlen=7)
+    for cu, n, msl in (([1, 3, 10], 10, None), ([0, 5, 4, 10], 10, None), ([0, 3, 9], 10, None),
+                       ([0, 3, 10], 10, 6), ([], 0, None)):
+        with pytest.raises(ValueError):
+            ops.check_cu_seqlens(torch.tensor(cu, dtype=torch.int32), n, max_seqlen=msl)
+    try:
+        ops.set_debug_checks(True)
+        assert ops._DEBUG_CHECKS is True
+    finally:
+        ops.set_debug_checks(False)
