@@ -6,7 +6,8 @@ module ``nano_vllm_extend_b200``.
 
 * ``ops``        tensor-level operators over the C ABI (libgdn_b200.so)
 * ``layer``      drop-in Qwen3_5GatedDeltaNet + ``install()`` into the engine
-* ``state_pool`` recurrent-state pools and slot free list (engine contract)
+* ``state_pool`` recurrent-state pools in the engine's layout (slot ids come from the
+                 engine's own free list)
 * ``parallel``   V-head sharding, TP linear layers, pipeline stage handoff
 * ``context``    per-step Context mirror
 """

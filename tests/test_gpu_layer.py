@@ -10,7 +10,6 @@ import pytest
 import torch
 
 import inputs as I
-from oracle import gdn_oracle as O
 
 pytestmark = pytest.mark.gpu
 DEV = "cuda:0"

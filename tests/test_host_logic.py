@@ -3,7 +3,6 @@ layer split, state-pool layout and slot lifecycle, layer construction and
 weight loading (no kernels run)."""
 import types
 
-import numpy as np
 import pytest
 import torch
 
