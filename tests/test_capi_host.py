@@ -20,8 +20,8 @@ def declared_symbols():
 def test_header_declares_the_path():
     syms = declared_symbols()
     for s in ("gdn_fused_g_beta", "gdn_conv_decode_step", "gdn_causal_conv_silu_varlen",
-              "gdn_conv_gate_varlen", "gdn_recurrent_inplace", "gdn_chunk_prefill_varlen", "gdn_rms_norm_gated",
-              "gdn_decode_fused", "gdn_abi_version", "gdn_last_error"):
+              "gdn_conv_gate_varlen", "gdn_recurrent_inplace", "gdn_chunk_prefill_varlen",
+              "gdn_rms_norm_gated", "gdn_decode_fused", "gdn_abi_version", "gdn_last_error"):
         assert s in syms
 
 
@@ -185,3 +185,17 @@ def test_decode_fused_host_validation(pkg):
     # rows with null pointers are rejected before any launch
     rc, msg = _call(pkg, "gdn_decode_fused", *_decode_fused_args())
     assert rc == L.GDN_ERR_INVALID_ARGUMENT and "null" in msg
+
+
+def test_integration_ctypes_stubs_match_the_signature_table(pkg):
+    """The ctypes bindings printed in INTEGRATION.md (what a maintainer of the
+    reference would paste) list the same argument types as the package's own
+    table, which the symbol test above ties to the header."""
+    L = pkg._lib
+    names = {L.vp: "vp", L.i32: "i32", L.i64: "i64", L.f32: "f32"}
+    doc = re.sub(r"#[^\n]*", "", open(os.path.join(ROOT, "INTEGRATION.md")).read())
+    stubs = re.findall(r"lib\.(gdn_\w+)\.argtypes = \[(.*?)\]", doc, flags=re.S)
+    assert len(stubs) >= 4
+    for name, body in stubs:
+        assert re.findall(r"\b(vp|i32|i64|f32)\b", body) == [names[t] for t in L.SIGNATURES[name]], \
+            name
